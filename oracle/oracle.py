@@ -1,0 +1,220 @@
+"""CPU ORACLE wrapper — test infrastructure only.
+
+ctypes bindings for ``oracle/ref_w8a32.c``, the C restatement of rust-ppocrv6's quantised
+recognition-head path (pack -> W8A32 projection -> softmax -> argmax -> CTC collapse).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s ``cpu_baseline`` /
+``--impl reference`` legs import this module, and only as the checker or as the timed CPU
+baseline. The product package ``rust_ppocrv6_b200`` never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
+_lib = None
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc, seconds) and return the .so path."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    src = os.path.join(_HERE, "ref_w8a32.c")
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        build()
+    L = ctypes.CDLL(_LIB_PATH)
+    L.oracle_cpu_has_avx2_fma.restype = _int
+    L.oracle_pack.argtypes = [_f32p, _i64, _i64, _i8p, _f32p]
+    L.oracle_matmul_quantized_b.argtypes = [_f32p, _i64, _i64, _i8p, _f32p, _i64, _i64, _vp, _i64, _f32p, _int]
+    L.oracle_matmul_quantized_b.restype = _int
+    L.oracle_matmul_quantized_b_colsplit.argtypes = [_f32p, _i64, _i64, _i8p, _f32p, _i64, _vp, _f32p, _int, _int]
+    L.oracle_softmax_rows_inplace.argtypes = [_f32p, _i64, _i64, _int]
+    L.oracle_softmax_general.argtypes = [_f32p, _f32p, _i64, _i64, _i64]
+    L.oracle_find_argmax.argtypes = [_f32p, _i64, _int, ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_float)]
+    L.oracle_find_argmax_scalar.argtypes = [_f32p, _i64, ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_float)]
+    L.oracle_ctc_collapse.argtypes = [_i32p, _f32p, _i64p, _i64, _i32p, _i64p, _f32p]
+    L.oracle_ctc_collapse.restype = _i64
+    L.oracle_head_decode.argtypes = [_f32p, _i64p, _i64, _i64, _i8p, _f32p, _i64, _vp, _i32p, _f32p, _vp, _vp,
+                                     _int, _int]
+    L.oracle_head_decode_one_line.argtypes = [_f32p, _i64, _i64, _i8p, _f32p, _i64, _vp, _i32p, _f32p, _f32p,
+                                              _int, _int]
+    L.oracle_matmul_f32_transposed_b.argtypes = [_f32p, _i64, _i64, _f32p, _i64, _vp, _f32p]
+    L.oracle_exp_poly.argtypes = [ctypes.c_float]
+    L.oracle_exp_poly.restype = ctypes.c_float
+    _lib = L
+    return L
+
+
+def _c(x, dt):
+    return np.ascontiguousarray(x, dtype=dt)
+
+
+def _ptr(x):
+    return None if x is None else x.ctypes.data_as(ctypes.c_void_p)
+
+
+def has_avx2() -> bool:
+    return bool(lib().oracle_cpu_has_avx2_fma())
+
+
+def pack(w_t: np.ndarray):
+    """QuantizedWeight::from_f32_transposed (src/ops/matmul.rs:1173-1202): w_t [n,k] -> (q int8 [n,k], scales f32 [n])."""
+    w_t = _c(w_t, np.float32)
+    n, k = w_t.shape
+    q = np.empty((n, k), np.int8)
+    s = np.empty(n, np.float32)
+    lib().oracle_pack(w_t, n, k, q, s)
+    return q, s
+
+
+def matmul_quantized_b(a: np.ndarray, q: np.ndarray, scales: np.ndarray, bias=None, use_avx2: bool = True):
+    """matmul_quantized_b (src/ops/matmul.rs:1204-1336), serial per-row schedule.
+
+    a is [..., k]; returns [..., n]. Raises ValueError where the reference returns
+    OcrError::OperatorError (K mismatch :1227-1232, bias length :1288-1295).
+    """
+    a = _c(a, np.float32)
+    n, k = q.shape
+    if a.ndim < 1:
+        raise ValueError("MatMulQuantizedB: Operand must have valid dimensions")
+    lead = a.shape[:-1]
+    rows = int(np.prod(lead)) if lead else 1
+    b = None if bias is None else _c(bias, np.float32).reshape(-1)
+    out = np.empty(lead + (n,), np.float32)
+    rc = lib().oracle_matmul_quantized_b(a.reshape(rows, a.shape[-1]), rows, a.shape[-1], _c(q, np.int8),
+                                         _c(scales, np.float32), n, k, _ptr(b), 0 if b is None else b.size,
+                                         out.reshape(rows, n), int(use_avx2))
+    if rc != 0:
+        raise ValueError("MatMulQuantizedB: inner dimension or bias length mismatch")
+    return out
+
+
+def matmul_quantized_b_colsplit(a, q, scales, bias=None, threads=1, use_avx2=True):
+    a = _c(a, np.float32)
+    n, k = q.shape
+    rows = a.shape[0]
+    b = None if bias is None else _c(bias, np.float32)
+    out = np.empty((rows, n), np.float32)
+    lib().oracle_matmul_quantized_b_colsplit(a, rows, k, _c(q, np.int8), _c(scales, np.float32), n, _ptr(b), out,
+                                             int(threads), int(use_avx2))
+    return out
+
+
+def softmax_lastaxis(x: np.ndarray, use_avx2: bool = True) -> np.ndarray:
+    """softmax_inplace over the last axis (src/ops/softmax.rs:199-285), on a copy."""
+    y = np.array(x, dtype=np.float32, copy=True, order="C")
+    if y.size == 0:
+        return y
+    n = y.shape[-1]
+    lib().oracle_softmax_rows_inplace(y.reshape(-1, n), y.size // n, n, int(use_avx2))
+    return y
+
+
+def softmax_general(x: np.ndarray, axis: int) -> np.ndarray:
+    """The inner_size > 1 path of softmax (src/ops/softmax.rs:143-196)."""
+    x = _c(x, np.float32)
+    axis = axis % x.ndim
+    outer = int(np.prod(x.shape[:axis])) if axis else 1
+    inner = int(np.prod(x.shape[axis + 1:])) if axis + 1 < x.ndim else 1
+    out = np.empty_like(x)
+    lib().oracle_softmax_general(x.reshape(-1), out.reshape(-1), outer, x.shape[axis], inner)
+    return out
+
+
+def find_argmax(x: np.ndarray, use_avx2: bool = True):
+    x = _c(x, np.float32)
+    i, v = _i64(), ctypes.c_float()
+    lib().oracle_find_argmax(x, x.size, int(use_avx2), ctypes.byref(i), ctypes.byref(v))
+    return int(i.value), float(v.value)
+
+
+def find_argmax_scalar(x: np.ndarray):
+    x = _c(x, np.float32)
+    i, v = _i64(), ctypes.c_float()
+    lib().oracle_find_argmax_scalar(x, x.size, ctypes.byref(i), ctypes.byref(v))
+    return int(i.value), float(v.value)
+
+
+def ctc_collapse(idx: np.ndarray, prob: np.ndarray, line_offsets: np.ndarray):
+    """Collapse + score of CtcDecoder::decode_batch (src/postprocess/ctc.rs:144-169).
+
+    Returns (list of int32 token arrays, f32 scores [n_lines])."""
+    idx = _c(idx, np.int32)
+    prob = _c(prob, np.float32)
+    off = _c(line_offsets, np.int64)
+    n_lines = off.size - 1
+    tokens = np.empty(max(idx.size, 1), np.int32)
+    toff = np.empty(n_lines + 1, np.int64)
+    scores = np.empty(max(n_lines, 0), np.float32)
+    lib().oracle_ctc_collapse(idx, prob, off, n_lines, tokens, toff, scores)
+    return [tokens[toff[l]:toff[l + 1]].copy() for l in range(n_lines)], scores
+
+
+def head_decode(a, line_offsets, q, scales, bias, threads=1, use_avx2=True, want_logits=False, want_gap=False):
+    """The whole head per timestep row: MatMul.12 (+ folded bias) -> Softmax.2 -> argmax.
+
+    a [M,k] with lines at line_offsets; returns dict(idx int32[M], prob f32[M], logits?, gap?).
+    """
+    a = _c(a, np.float32)
+    off = _c(line_offsets, np.int64)
+    n, k = q.shape
+    m = a.shape[0]
+    idx = np.empty(m, np.int32)
+    prob = np.empty(m, np.float32)
+    logits = np.empty((m, n), np.float32) if want_logits else None
+    gap = np.empty(m, np.float32) if want_gap else None
+    b = None if bias is None else _c(bias, np.float32)
+    lib().oracle_head_decode(a, off, off.size - 1, k, _c(q, np.int8), _c(scales, np.float32), n, _ptr(b), idx,
+                             prob, _ptr(logits), _ptr(gap), int(threads), int(use_avx2))
+    out = {"idx": idx, "prob": prob}
+    if want_logits:
+        out["logits"] = logits
+    if want_gap:
+        out["gap"] = gap
+    return out
+
+
+def head_decode_one_line(a, q, scales, bias, scratch, threads=1, use_avx2=True):
+    a = _c(a, np.float32)
+    n, k = q.shape
+    m = a.shape[0]
+    idx = np.empty(m, np.int32)
+    prob = np.empty(m, np.float32)
+    b = None if bias is None else _c(bias, np.float32)
+    lib().oracle_head_decode_one_line(a, m, k, _c(q, np.int8), _c(scales, np.float32), n, _ptr(b), idx, prob,
+                                      scratch, int(threads), int(use_avx2))
+    return idx, prob
+
+
+def matmul_f32_transposed_b(a, b_t, bias=None):
+    a = _c(a, np.float32)
+    b_t = _c(b_t, np.float32)
+    rows, k = a.reshape(-1, a.shape[-1]).shape
+    n = b_t.shape[0]
+    out = np.empty(a.shape[:-1] + (n,), np.float32)
+    b = None if bias is None else _c(bias, np.float32)
+    lib().oracle_matmul_f32_transposed_b(a.reshape(rows, k), rows, k, b_t, n, _ptr(b), out.reshape(rows, n))
+    return out
+
+
+def exp_poly(x: float) -> float:
+    return float(lib().oracle_exp_poly(float(x)))
