@@ -1,0 +1,350 @@
+"""Benchmark: decoded timesteps/s of the fused W8A32 recognition head on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg3]
+
+One step = one pass of the hot path (MatMul.12 + Add.204 -> Softmax.2 -> per-timestep
+argmax) over one batch. Default workload cfg2: 1024 text lines x T=120 timesteps per GPU
+(M = 122,880 rows, K = 120, N = 18,710), weak scaling over N GPUs (one process per GPU
+under torchrun; lines are independent, so no collective is in the data path; a MAX
+all-reduce of the per-rank device times is the only communication). --workload cfg3
+instead shards one global 8192-line ragged batch over the ranks (strong scaling).
+
+`value`  device-resident throughput: inputs already in HBM (rotating over enough copies to
+         exceed 2x the 126 MB L2), CUDA events on the launching stream, max over ranks.
+`e2e`    the same metric through the public host API (rh_head_decode on pinned host
+         memory): H2D of the features and D2H of idx/prob inside the timed region.
+--impl reference  times the reference algorithm's CPU implementation (the C restatement in
+         oracle/, all host threads, lines spread over workers like src/pipeline.rs:417-427)
+         on bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+K_DIM = 120
+N_CLASSES = 18710
+FLOP_PER_ROW = 2 * K_DIM * N_CLASSES  # algorithmic FLOPs per timestep (2*K*N)
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "W8A32 rec-head decoded timesteps/s (MatMul.12+Add.204 -> Softmax.2 -> argmax)"
+UNIT = "timesteps/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2")
+    ap.add_argument("--cpu-sample-lines", type=int, default=48)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def workload_for(name: str, world: int, rank: int):
+    """(line_offsets of this rank's lines rebased to 0, rows, global rows, description)."""
+    from rust_ppocrv6_b200 import workloads
+
+    if name == "cfg2":
+        off = workloads.uniform_offsets(1024, 120)
+        desc = f"cfg2: 1024 lines x T=120 per GPU (M=122880/GPU), K=120, N=18710; global batch {1024 * world} lines"
+        return off, int(off[-1]), int(off[-1]) * world, desc, "weak"
+    rng = np.random.default_rng(workloads.SEED + 3)
+    off_all = workloads.ragged_offsets(rng, 8192)
+    l0, l1 = workloads.shard_lines(off_all, world, rank)
+    off = off_all[l0:l1 + 1] - off_all[l0]
+    desc = f"cfg3: 8192 ragged lines T~U{{10..120}} (M={int(off_all[-1])}) sharded over {world} GPU(s)"
+    return off, int(off[-1]), int(off_all[-1]), desc, "strong"
+
+
+def synth(rows: int, seed: int):
+    rng = np.random.default_rng(seed)
+    return rng.standard_normal((rows, K_DIM), dtype=np.float32)
+
+
+def head_weights():
+    from rust_ppocrv6_b200 import workloads
+
+    rng = np.random.default_rng(workloads.SEED + 2)
+    return workloads.head_weights(rng)
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception:
+            self._ok = False
+
+    def _run(self):
+        nv = self._nv
+        names = {
+            "hw_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksThrottleReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(nv, "nvmlClocksThrottleReasonSwPowerCap", 0x4),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                for k, bit in names.items():
+                    if r & bit:
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self._ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self._ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def measured_peak_tflops():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured bf16 dense (MEASURED_PEAKS.json, burst)"
+    except Exception:
+        return 1590.0, "fallback 1.59 PFLOP/s bf16 dense"
+
+
+def profiled_traffic():
+    try:
+        with open(os.path.join(ROOT, "profiles", "head_kernel_traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+def cpu_reference(lines_off: np.ndarray, x: np.ndarray, w_t, bias, sample_lines: int, reps: int = 1):
+    """Times the oracle port (the reference's AVX2 path, restated) on `sample_lines` lines
+    of the workload with every host thread. Returns (timesteps/s, threads, rows, seconds)."""
+    from oracle import oracle
+
+    q, s = oracle.pack(w_t)
+    nl = min(sample_lines, lines_off.size - 1)
+    off = lines_off[:nl + 1]
+    rows = int(off[-1])
+    xs = np.ascontiguousarray(x[:rows])
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    oracle.head_decode(xs[: int(off[1])], off[:2], q, s, bias, threads=threads)  # warm caches
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.head_decode(xs, off, q, s, bias, threads=threads)
+    dt = time.perf_counter() - t0
+    return rows * reps / dt, threads, rows, dt
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    off, rows, _, desc, _ = workload_for(args.workload, 1, 0)
+    w_t, bias = head_weights()
+    x = synth(min(rows, int(off[min(args.cpu_sample_lines, off.size - 1)])), 1234)
+    from oracle import oracle
+
+    q, s = oracle.pack(w_t)
+    nl = min(args.cpu_sample_lines, off.size - 1)
+    soff = off[:nl + 1]
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    for _ in range(max(args.warmup, 0)):
+        oracle.head_decode(x, soff, q, s, bias, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.head_decode(x, soff, q, s, bias, threads=threads)
+    dt = time.perf_counter() - t0
+    srows = int(soff[-1])
+    value = srows * args.steps / dt
+    sample = f"{nl} lines x T=120 ({srows} timesteps) of {desc.split(';')[0]} per step"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "none (host CPU)", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) features, N(0,0.05^2) weights, N(0,0.01^2) bias)",
+        "config": {"workload": desc, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+
+    import torch
+
+    import rust_ppocrv6_b200 as rh
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    off, rows, global_rows, desc, scaling = workload_for(args.workload, world, rank)
+    w_t, bias = head_weights()
+    ctx = rh.Context(devices=[local])
+    qw = rh.QuantizedWeight.from_f32_transposed(w_t, ctx=ctx, bias=bias)
+
+    x_host = synth(rows, 1000 + rank)
+    x_bytes = x_host.nbytes
+    n_copies = max(2, int(np.ceil(2 * L2_BYTES / max(x_bytes, 1))) + 1)
+    n_copies = min(n_copies, 64)
+    xs = [torch.from_numpy(x_host).cuda()]
+    for i in range(1, n_copies):
+        xs.append(xs[0].roll(i, dims=0).contiguous())  # distinct buffers, same statistics
+    idx = torch.empty(rows, dtype=torch.int32, device="cuda")
+    prob = torch.empty(rows, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+
+    def step(i):
+        rh.head_decode_device(qw, xs[i % n_copies].data_ptr(), rows, idx.data_ptr(), prob.data_ptr(), sptr)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    ctx.sync()
+    l0 = ctx.launch_count(0)
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ctx.sync()
+    launches = ctx.launch_count(0) - l0
+    dev_ms = ev0.elapsed_time(ev1)
+    dev_ms_max = max_over_ranks(dev_ms)
+    value = global_rows * args.steps / (dev_ms_max / 1e3)
+    ms_per_step = dev_ms_max / args.steps
+
+    # end to end through the public host API (pinned host buffers, H2D + D2H inside)
+    x_pin = torch.from_numpy(x_host).pin_memory()
+    idx_h = torch.empty(rows, dtype=torch.int32).pin_memory()
+    prob_h = torch.empty(rows, dtype=torch.float32).pin_memory()
+    import ctypes
+
+    lib = rh.load()
+
+    def e2e_step():
+        rh._lib.check(lib.rh_head_decode(ctx.handle, qw.handle, ctypes.c_void_p(x_pin.data_ptr()), rows, K_DIM,
+                                         ctypes.c_void_p(idx_h.data_ptr()), ctypes.c_void_p(prob_h.data_ptr())))
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e_value = global_rows * args.steps / e2e_s
+
+    # roofline of the dominant kernel (the fused head; the split merge is <1 % of a step)
+    peak, peak_src = measured_peak_tflops()
+    achieved = FLOP_PER_ROW * rows / (dev_ms / args.steps / 1e3) / 1e12
+    traffic = profiled_traffic()
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "peak_source": peak_src,
+                "traffic": None if traffic is None else traffic["bytes_per_launch_cfg2"],
+                "tf32_equiv_frac": achieved / (peak / 2),
+                "note": "achieved = 2*K*N*rows per step / device time per step (head + merge kernels)"}
+
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": scaling,
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) features, N(0,0.05^2) weights, N(0,0.01^2) bias; no public dataset)",
+        "config": {"workload": desc, "timesteps_per_step": global_rows, "parallelism": f"lines sharded x{world}",
+                   "l2": f"inputs rotate over {n_copies} device copies ({n_copies * x_bytes / 2**20:.0f} MiB > 2x L2)"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x_bytes),
+                "d2h_bytes_per_step": int(rows * 8), "ms_per_step": e2e_s * 1e3 / args.steps},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, srows, dt = cpu_reference(off, x_host, w_t, bias, args.cpu_sample_lines)
+        out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                               "sample": f"{srows} timesteps ({args.cpu_sample_lines} lines of the workload), "
+                                         f"{dt:.2f} s wall"}
+    qw.free()
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+/*
+ * rechead.h — C ABI of the B200-native (sm_100a) quantised recognition head of
+ * rust-ppocrv6: the per-class symmetric INT8 W8A32 projection of SVTR features onto the CTC
+ * vocabulary (graph node MatMul.12 with the folded bias Add.204), softmax (Softmax.2) and
+ * the per-timestep greedy argmax that CTC decoding consumes.
+ *
+ * Every entry point replaces one call the Rust engine makes today; each declaration cites
+ * the reference item it stands in for (paths inside the rust-ppocrv6 project).
+ *
+ * Conventions
+ *  - Plain pointers and sizes; no ownership passes except through the opaque handles.
+ *  - Functions return RH_OK (0) or an RH_ERR_* code. rh_last_error() then describes the
+ *    failure of the calling thread's most recent call. RH_ERR_INVALID_ARG is the analogue of
+ *    the reference's OcrError::OperatorError (src/error.rs:4-27); nothing here aborts the
+ *    process (the reference keeps panic = "abort" off for embedders, Cargo.toml:41-45).
+ *  - "Host" entry points take host memory (pinned or pageable) and return when the results
+ *    are in host memory. "_device" entry points take device memory of one context device
+ *    and a cudaStream_t (as void*), enqueue asynchronously and report device-side failures
+ *    at the next rh_sync() on that device.
+ *  - Requires an sm_100 (B200-class) GPU. There is no CPU fallback: rh_ctx_create fails
+ *    with RH_ERR_NO_DEVICE / RH_ERR_UNSUPPORTED when no such device is present.
+ *  - Calls on one context are serialised per device and are safe from many threads (the
+ *    engine calls the head from up to rec_batch_threads Rayon workers, src/pipeline.rs:417-427).
+ */
+#ifndef RECHEAD_H
+#define RECHEAD_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RH_OK 0
+#define RH_ERR_INVALID_ARG 1  /* bad shape, length or pointer: OcrError::OperatorError */
+#define RH_ERR_CUDA 2         /* a CUDA runtime call failed */
+#define RH_ERR_TIMEOUT 3      /* a kernel's bounded wait ran out; the context stays usable */
+#define RH_ERR_UNSUPPORTED 4  /* K > 128, or a device that is not sm_100 */
+#define RH_ERR_NO_DEVICE 5    /* no CUDA device */
+#define RH_ERR_DEVICE_FAULT 6 /* a device shard failed and no healthy device could redo it */
+
+typedef struct rh_ctx rh_ctx;
+typedef struct rh_weight rh_weight;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int rh_version(void);
+
+/* Number of visible CUDA devices. */
+int rh_device_count(int *count);
+
+/* Message for the calling thread's most recent failed call ("" if none). Never NULL. */
+const char *rh_last_error(void);
+
+/*
+ * Creates a context over `n_devices` CUDA devices (devices == NULL: device 0 only). Each
+ * device gets its own stream, status word and scratch. Batched host calls shard their lines
+ * over these devices. Replaces the engine's recognition worker pool for this head
+ * (OcrEngine::with_config rec_pool, src/pipeline.rs:232-251).
+ */
+int rh_ctx_create(const int *devices, int n_devices, rh_ctx **out);
+void rh_ctx_destroy(rh_ctx *ctx);
+int rh_ctx_num_devices(const rh_ctx *ctx);
+/* Upper bound on any device-side wait, in milliseconds (default 2000). */
+int rh_ctx_set_timeout_ms(rh_ctx *ctx, int timeout_ms);
+
+/*
+ * Quantises and packs the transposed head weight w_nk [n][k] (row j = class j, as built by
+ * the load-time transpose in src/engine/model.rs:565-605) on every context device, with the
+ * bias folded in (bias may be NULL; otherwise bias_len must equal n, as
+ * src/ops/matmul.rs:1288-1295 requires). Bit-exact with QuantizedWeight::from_f32_transposed
+ * (src/ops/matmul.rs:1173-1202) as called by Model::quantize_matmul_weights
+ * (src/engine/model.rs:628-638) when OcrEngineConfig.quantize_rec_head is set
+ * (src/pipeline.rs:197-199). Keeps no host copy of the FP32 weight. 1 <= k <= 128.
+ */
+int rh_weight_pack(rh_ctx *ctx, const float *w_nk, int64_t n, int64_t k, const float *bias, int64_t bias_len,
+                   rh_weight **out);
+
+/* Replaces the folded bias (NULL: no bias). bias_len must equal n. The MatMul arm passes the
+ * folded Add.204 bias on every call (src/engine/model.rs:1248-1252, :1261-1262). */
+int rh_weight_set_bias(rh_ctx *ctx, rh_weight *w, const float *bias, int64_t bias_len);
+
+/* Copies out QuantizedWeight::data (int8 [n][k]) and ::scales (f32 [n]) from the first
+ * context device (src/ops/matmul.rs:1165-1171); either pointer may be NULL. */
+int rh_weight_export(rh_ctx *ctx, const rh_weight *w, int8_t *q, float *scales);
+
+/* Copies out the tensor-core image of the weight (n_chunks * 32768 bytes, n_chunks =
+ * ceil(n/128)) and the per-class (scale, bias) table (n_chunks * 128 float pairs). */
+int rh_weight_export_image(rh_ctx *ctx, const rh_weight *w, uint8_t *tiles, float *colp);
+
+int rh_weight_dims(const rh_weight *w, int64_t *n, int64_t *k);
+
+/* Device bytes held per device by the packed weight (Model::weight_footprint_bytes,
+ * src/engine/model.rs:651-667, for the head). */
+int64_t rh_weight_device_bytes(const rh_weight *w);
+
+void rh_weight_free(rh_weight *w);
+
+/*
+ * out[r][j] = (sum_i a[r][i] * q[j][i]) * scale[j] + bias[j] for r < rows, j < n: the
+ * literal drop-in for matmul_quantized_b (src/ops/matmul.rs:1204-1336) as dispatched by
+ * the MatMul arm for MatMul.12 (src/engine/model.rs:1245-1272). `k` must equal the
+ * weight's K (the check at src/ops/matmul.rs:1227-1232). a is [rows][k], out [rows][n],
+ * both host memory. rows == 0 is a no-op.
+ */
+int rh_matmul_quantized_b(rh_ctx *ctx, const rh_weight *w, const float *a, int64_t rows, int64_t k, float *out);
+
+/*
+ * The fused head: for each timestep row r of a [rows][k], the class with the largest
+ * probability after softmax over all n classes (first index on ties) and that probability,
+ * i.e. matmul_quantized_b -> softmax_inplace (src/ops/softmax.rs:199-285, dispatched by the
+ * Softmax arm src/engine/model.rs:1286-1302) -> find_argmax (src/postprocess/ctc.rs:178-258)
+ * as CtcDecoder::decode_batch applies it per timestep (src/postprocess/ctc.rs:144-149).
+ * The [rows][n] logits never leave the GPU. Host memory; runs on the first device.
+ */
+int rh_head_decode(rh_ctx *ctx, const rh_weight *w, const float *a, int64_t rows, int64_t k, int32_t *idx,
+                   float *prob);
+
+/*
+ * rh_head_decode over a batch of text lines packed densely: line l owns rows
+ * [line_offsets[l], line_offsets[l+1]) of a. Lines are split into contiguous shards of
+ * balanced timestep count, one per context device, run concurrently, and gathered into
+ * idx/prob (no collective: only the per-row results come back). Replaces the per-line
+ * Rayon fan-out of OcrEngine::recognize (src/pipeline.rs:395-436) for this head. A shard
+ * whose device fails is redone on a healthy device; results do not depend on the device.
+ */
+int rh_head_decode_lines(rh_ctx *ctx, const rh_weight *w, const float *a, const int64_t *line_offsets,
+                         int64_t n_lines, int64_t k, int32_t *idx, float *prob);
+
+/* Device-memory forms on context device `slot` (0-based) and `stream` (cudaStream_t, NULL =
+ * the legacy default stream). Asynchronous; failures surface at rh_sync(). */
+int rh_head_decode_device(rh_ctx *ctx, const rh_weight *w, int slot, const float *d_a, int64_t rows, int32_t *d_idx,
+                          float *d_prob, void *stream);
+int rh_matmul_quantized_b_device(rh_ctx *ctx, const rh_weight *w, int slot, const float *d_a, int64_t rows,
+                                 float *d_out, void *stream);
+
+/* Waits for all work on device `slot` (slot < 0: every device) and reports device-side
+ * failures (RH_ERR_TIMEOUT) recorded since the previous rh_sync. */
+int rh_sync(rh_ctx *ctx, int slot);
+
+/* Number of head-kernel launches (head + merge + pack) issued on `slot` since creation. */
+int64_t rh_launch_count(const rh_ctx *ctx, int slot);
+
+/*
+ * CTC greedy collapse on per-timestep (idx, prob): the loop of CtcDecoder::decode_batch
+ * (src/postprocess/ctc.rs:144-169). For line l (timesteps [line_offsets[l],
+ * line_offsets[l+1])) emit idx[t] when idx[t] != 0 (blank) and idx[t] != idx[t-1] (repeat;
+ * the previous index starts at 0 for each line). tokens receives the emitted class indices
+ * of all lines back to back (capacity >= line_offsets[n_lines] - line_offsets[0]);
+ * token_offsets[l]..token_offsets[l+1] delimit line l (n_lines + 1 entries); scores[l] is
+ * the f32 mean of the emitted probabilities (0 when none). Returns the number of tokens, or
+ * -1 on invalid arguments. Host-only; needs no device.
+ */
+int64_t rh_ctc_collapse(const int32_t *idx, const float *prob, const int64_t *line_offsets, int64_t n_lines,
+                        int32_t *tokens, int64_t *token_offsets, float *scores);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RECHEAD_H */

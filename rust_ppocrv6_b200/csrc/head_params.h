@@ -1,0 +1,67 @@
+// Launch parameters shared by the host dispatch (rechead_abi.cu) and the kernels
+// (rechead_kernels.cu). Plain C types only.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace rh {
+
+constexpr int kBlockM = 128;                  // timestep rows per work unit (one TMEM lane each)
+constexpr int kBlockN = 128;                  // classes per weight tile / accumulator
+constexpr int kPadK = 128;                    // K extent of a weight tile (K <= 128 supported)
+constexpr int kTileBytes = kBlockN * kPadK * 2;  // one fp16 weight tile: 32 KB
+constexpr int kStages = 4;                    // weight-tile ring depth in shared memory
+constexpr int kHeadThreads = 512;             // 16 warps, see head_kernel
+
+// Device status word bits (status[0]); status[1] records which wait gave up.
+constexpr int kDevTimeout = 1;
+// Test-only: the weight producer never fills its stages, so every consumer's bounded wait
+// runs out and the kernel must return kDevTimeout with the context intact.
+constexpr int kDebugStallProducer = 1;
+
+struct HeadParams {
+    const float* a;            // [m][k] timestep features (rows packed densely)
+    long long m;
+    int k;
+    int n;
+    int n_chunks;              // ceil(n / 128)
+    int hi_steps;              // MMA K-steps of the high fp16 part of A
+    int lo_steps;              // MMA K-steps of the low fp16 part of A
+    int merged_tail;           // 1: hi step hi_steps-1 also carries lo's last 8 K values
+    const uint8_t* btiles;     // n_chunks * 32 KB, fp16 weight tiles in the smem image order
+    const float2* colp;        // n_chunks * 128 (scale, bias); padded columns (0, -inf)
+    int n_mblocks;             // ceil(m / 128)
+    int n_splits;              // class-range splits per row block
+    int chunks_per_split;
+    int32_t* idx;              // fused, n_splits == 1: argmax class per row
+    float* prob;               // fused, n_splits == 1: max softmax probability per row
+    float4* partial;           // fused, n_splits > 1: [n_splits][m] (max, sum, idx bits, 0)
+    float* logits;             // logits variant: [m][n]
+    int* status;               // [2]
+    unsigned long long timeout_ns;
+    int debug_flags;
+};
+
+struct PackParams {
+    const float* w;            // [n][k] transposed head weight
+    const float* bias;         // [n] or null
+    int n;
+    int k;
+    int n_pad;                 // n_chunks * 128
+    int merged_tail;
+    int tail_step;             // index of the last hi K-step (ceil(k/16) - 1)
+    int8_t* q;                 // [n][k] canonical int8 (QuantizedWeight::data)
+    float* scales;             // [n]
+    uint8_t* btiles;           // n_pad/128 tiles of 32 KB
+    float2* colp;              // [n_pad]
+};
+
+// Kernel launchers (rechead_kernels.cu).
+cudaError_t launch_pack(const PackParams& p, cudaStream_t stream);
+cudaError_t launch_head(const HeadParams& p, bool emit_logits, int grid, cudaStream_t stream);
+cudaError_t launch_merge(const float4* partial, int n_splits, long long m, int32_t* idx, float* prob,
+                         cudaStream_t stream);
+size_t head_smem_bytes();
+cudaError_t head_kernel_setup();
+
+}  // namespace rh

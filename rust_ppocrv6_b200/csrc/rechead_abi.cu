@@ -1,0 +1,632 @@
+// Host side of the C ABI declared in include/rechead.h: contexts (one stream, status word
+// and scratch per device), packed weights, work planning, launches, multi-device sharding of
+// line batches and the host CTC collapse. No CPU fallback exists: every compute entry point
+// runs the sm_100a kernels of rechead_kernels.cu or fails.
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "head_params.h"
+#include "rechead.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+#define RH_CUDA(call)                                                                         \
+    do {                                                                                      \
+        cudaError_t e_ = (call);                                                              \
+        if (e_ != cudaSuccess) return fail(RH_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap && p) return cudaSuccess;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        cudaError_t e = cudaMalloc(&p, std::max<size_t>(bytes, 256));
+        if (e == cudaSuccess) cap = std::max<size_t>(bytes, 256);
+        return e;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+};
+
+struct Slot {
+    int device = 0;
+    int sms = 0;
+    cudaStream_t stream = nullptr;
+    int* d_status = nullptr;
+    DevBuf a, idx, prob, out, partial;
+    std::mutex mu;
+    int64_t launches = 0;
+};
+
+struct Geometry {
+    int n_chunks, hi_steps, lo_steps, merged, tail_step;
+};
+
+Geometry geometry(int64_t n, int64_t k) {
+    Geometry g;
+    g.n_chunks = (int)((n + rh::kBlockN - 1) / rh::kBlockN);
+    const int k16 = (int)((k + 15) / 16);
+    g.tail_step = k16 - 1;
+    const int rem = (int)(k - 16 * g.tail_step);  // 1..16 values in the last K step
+    g.merged = rem <= 8 ? 1 : 0;
+    g.hi_steps = k16;
+    g.lo_steps = g.merged ? k16 - 1 : k16;
+    return g;
+}
+
+// Chooses how many class-range splits each 128-row block gets so that the persistent grid
+// is evenly loaded: cost = waves * (chunks per unit + per-unit overhead).
+void plan(int64_t m, int n_chunks, int sms, int& n_mblocks, int& n_splits, int& cps, int& grid) {
+    n_mblocks = (int)((m + rh::kBlockM - 1) / rh::kBlockM);
+    double best = 1e300;
+    n_splits = 1;
+    cps = n_chunks;
+    for (int s = 1; s <= n_chunks; ++s) {
+        const int c = (n_chunks + s - 1) / s;
+        const int s_eff = (n_chunks + c - 1) / c;
+        const long long units = (long long)n_mblocks * s_eff;
+        const long long waves = (units + sms - 1) / sms;
+        const double cost = (double)waves * (c + 2.0);
+        if (cost < best - 1e-9) {
+            best = cost;
+            n_splits = s_eff;
+            cps = c;
+        }
+    }
+    const long long units = (long long)n_mblocks * n_splits;
+    grid = (int)std::min<long long>(units, sms);
+}
+
+std::vector<int> injected_fault_slots() {
+    std::vector<int> v;
+    const char* s = std::getenv("RH_FAULT_DEVICE");
+    if (!s) return v;
+    std::string str(s);
+    size_t pos = 0;
+    while (pos < str.size()) {
+        size_t e = str.find(',', pos);
+        if (e == std::string::npos) e = str.size();
+        if (e > pos) v.push_back(std::atoi(str.substr(pos, e - pos).c_str()));
+        pos = e + 1;
+    }
+    return v;
+}
+
+}  // namespace
+
+struct rh_ctx {
+    std::vector<std::unique_ptr<Slot>> slots;
+    unsigned long long timeout_ns = 2000000000ull;
+};
+
+struct rh_weight {
+    int64_t n = 0, k = 0;
+    Geometry g{};
+    struct Per {
+        int device = 0;
+        int8_t* q = nullptr;
+        float* scales = nullptr;
+        uint8_t* tiles = nullptr;
+        float2* colp = nullptr;
+    };
+    std::vector<Per> per;
+    std::vector<float> host_scales;  // QuantizedWeight::scales, kept to rebuild the bias table
+};
+
+namespace {
+
+int check_ctx(rh_ctx* ctx) {
+    if (!ctx || ctx->slots.empty()) return fail(RH_ERR_INVALID_ARG, "null or empty context");
+    return RH_OK;
+}
+
+// Enqueues the head (and the split merge) for rows [0, rows) of d_a on `stream`.
+int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per& pw, const float* d_a, int64_t rows,
+                 int32_t* d_idx, float* d_prob, float* d_logits, bool emit_logits, cudaStream_t stream) {
+    if (rows <= 0) return RH_OK;
+    int n_mblocks, n_splits, cps, grid;
+    plan(rows, w->g.n_chunks, s.sms, n_mblocks, n_splits, cps, grid);
+    rh::HeadParams p{};
+    p.a = d_a;
+    p.m = rows;
+    p.k = (int)w->k;
+    p.n = (int)w->n;
+    p.n_chunks = w->g.n_chunks;
+    p.hi_steps = w->g.hi_steps;
+    p.lo_steps = w->g.lo_steps;
+    p.merged_tail = w->g.merged;
+    p.btiles = pw.tiles;
+    p.colp = pw.colp;
+    p.n_mblocks = n_mblocks;
+    p.n_splits = n_splits;
+    p.chunks_per_split = cps;
+    p.idx = d_idx;
+    p.prob = d_prob;
+    p.logits = d_logits;
+    p.status = s.d_status;
+    p.timeout_ns = ctx->timeout_ns;
+    p.debug_flags = 0;
+    if (const char* dbg = std::getenv("RH_DEBUG_FLAGS")) p.debug_flags = std::atoi(dbg);
+    if (!emit_logits && n_splits > 1) {
+        RH_CUDA(s.partial.ensure((size_t)n_splits * (size_t)rows * sizeof(float4)));
+        p.partial = static_cast<float4*>(s.partial.p);
+    }
+    RH_CUDA(rh::launch_head(p, emit_logits, grid, stream));
+    s.launches++;
+    if (!emit_logits && n_splits > 1) {
+        RH_CUDA(rh::launch_merge(p.partial, n_splits, rows, d_idx, d_prob, stream));
+        s.launches++;
+    }
+    return RH_OK;
+}
+
+int read_status(Slot& s) {
+    int st[2] = {0, 0};
+    RH_CUDA(cudaMemcpy(st, s.d_status, sizeof(st), cudaMemcpyDeviceToHost));
+    if (st[0] != 0) {
+        RH_CUDA(cudaMemset(s.d_status, 0, 2 * sizeof(int)));
+        if (st[0] & rh::kDevTimeout)
+            return fail(RH_ERR_TIMEOUT, "device wait timed out (site " + std::to_string(st[1]) +
+                                            "); the kernel gave up and the context is still usable");
+        return fail(RH_ERR_CUDA, "device status " + std::to_string(st[0]));
+    }
+    return RH_OK;
+}
+
+const rh_weight::Per* weight_on(const rh_weight* w, int device) {
+    for (const auto& p : w->per)
+        if (p.device == device) return &p;
+    return nullptr;
+}
+
+// Host-memory head on one slot: H2D rows, kernels, D2H results, synchronise, check status.
+int run_host_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, int64_t rows, int32_t* idx,
+                     float* prob, float* logits) {
+    if (rows <= 0) return RH_OK;
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
+    const size_t a_bytes = (size_t)rows * (size_t)w->k * sizeof(float);
+    RH_CUDA(s.a.ensure(a_bytes));
+    RH_CUDA(cudaMemcpyAsync(s.a.p, a, a_bytes, cudaMemcpyHostToDevice, s.stream));
+    const bool emit_logits = logits != nullptr;
+    if (emit_logits) {
+        const size_t o_bytes = (size_t)rows * (size_t)w->n * sizeof(float);
+        RH_CUDA(s.out.ensure(o_bytes));
+        int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, nullptr, nullptr, (float*)s.out.p, true,
+                              s.stream);
+        if (rc) return rc;
+        RH_CUDA(cudaMemcpyAsync(logits, s.out.p, o_bytes, cudaMemcpyDeviceToHost, s.stream));
+    } else {
+        RH_CUDA(s.idx.ensure((size_t)rows * sizeof(int32_t)));
+        RH_CUDA(s.prob.ensure((size_t)rows * sizeof(float)));
+        int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, (int32_t*)s.idx.p, (float*)s.prob.p,
+                              nullptr, false, s.stream);
+        if (rc) return rc;
+        RH_CUDA(cudaMemcpyAsync(idx, s.idx.p, (size_t)rows * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
+        RH_CUDA(cudaMemcpyAsync(prob, s.prob.p, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+    }
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    return read_status(s);
+}
+
+int upload_colp(rh_weight* w, const float* bias) {
+    const int n_pad = w->g.n_chunks * rh::kBlockN;
+    std::vector<float2> colp(n_pad);
+    for (int j = 0; j < n_pad; ++j) {
+        if (j < w->n)
+            colp[j] = make_float2(w->host_scales[j], bias ? bias[j] : 0.0f);
+        else
+            colp[j] = make_float2(0.0f, -INFINITY);
+    }
+    for (auto& p : w->per) {
+        RH_CUDA(cudaSetDevice(p.device));
+        RH_CUDA(cudaMemcpy(p.colp, colp.data(), colp.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    }
+    return RH_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rh_version(void) { return 100; }
+
+const char* rh_last_error(void) { return g_err.c_str(); }
+
+int rh_device_count(int* count) {
+    if (!count) return fail(RH_ERR_INVALID_ARG, "count is null");
+    int c = 0;
+    cudaError_t e = cudaGetDeviceCount(&c);
+    if (e != cudaSuccess) c = 0;
+    *count = c;
+    return RH_OK;
+}
+
+int rh_ctx_create(const int* devices, int n_devices, rh_ctx** out) {
+    if (!out) return fail(RH_ERR_INVALID_ARG, "out is null");
+    *out = nullptr;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
+        return fail(RH_ERR_NO_DEVICE, "no CUDA device is visible; this library has no CPU path");
+    std::vector<int> devs;
+    if (!devices || n_devices <= 0)
+        devs.push_back(0);
+    else
+        devs.assign(devices, devices + n_devices);
+    auto ctx = std::make_unique<rh_ctx>();
+    if (const char* t = std::getenv("RH_TIMEOUT_MS")) ctx->timeout_ns = (unsigned long long)std::atoll(t) * 1000000ull;
+    for (int d : devs) {
+        if (d < 0 || d >= count) return fail(RH_ERR_INVALID_ARG, "device index out of range: " + std::to_string(d));
+        for (const auto& s : ctx->slots)
+            if (s->device == d) return fail(RH_ERR_INVALID_ARG, "device listed twice: " + std::to_string(d));
+        cudaDeviceProp prop;
+        RH_CUDA(cudaGetDeviceProperties(&prop, d));
+        if (prop.major != 10 || prop.minor != 0)
+            return fail(RH_ERR_UNSUPPORTED, std::string("device ") + std::to_string(d) + " (" + prop.name + ", sm_" +
+                                                std::to_string(prop.major) + std::to_string(prop.minor) +
+                                                ") is not sm_100; the kernels are built for sm_100a only");
+        auto s = std::make_unique<Slot>();
+        s->device = d;
+        s->sms = prop.multiProcessorCount;
+        RH_CUDA(cudaSetDevice(d));
+        RH_CUDA(rh::head_kernel_setup());
+        RH_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+        RH_CUDA(cudaMalloc(&s->d_status, 2 * sizeof(int)));
+        RH_CUDA(cudaMemset(s->d_status, 0, 2 * sizeof(int)));
+        ctx->slots.push_back(std::move(s));
+    }
+    *out = ctx.release();
+    return RH_OK;
+}
+
+void rh_ctx_destroy(rh_ctx* ctx) {
+    if (!ctx) return;
+    for (auto& s : ctx->slots) {
+        cudaSetDevice(s->device);
+        cudaStreamSynchronize(s->stream);
+        s->a.release();
+        s->idx.release();
+        s->prob.release();
+        s->out.release();
+        s->partial.release();
+        if (s->d_status) cudaFree(s->d_status);
+        if (s->stream) cudaStreamDestroy(s->stream);
+    }
+    delete ctx;
+}
+
+int rh_ctx_num_devices(const rh_ctx* ctx) { return ctx ? (int)ctx->slots.size() : 0; }
+
+int rh_ctx_set_timeout_ms(rh_ctx* ctx, int timeout_ms) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (timeout_ms <= 0) return fail(RH_ERR_INVALID_ARG, "timeout must be positive");
+    ctx->timeout_ns = (unsigned long long)timeout_ms * 1000000ull;
+    return RH_OK;
+}
+
+int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len,
+                   rh_weight** out) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!out || !w_nk) return fail(RH_ERR_INVALID_ARG, "null weight or output pointer");
+    *out = nullptr;
+    if (n < 1 || k < 1) return fail(RH_ERR_INVALID_ARG, "weight must be [n>=1][k>=1]");
+    if (k > rh::kPadK)
+        return fail(RH_ERR_UNSUPPORTED, "K = " + std::to_string(k) + " exceeds the supported maximum of 128");
+    if (n > (int64_t)1 << 24) return fail(RH_ERR_UNSUPPORTED, "n too large");
+    if (bias && bias_len != n)
+        return fail(RH_ERR_INVALID_ARG,
+                    "bias has " + std::to_string(bias_len) + " elements but n is " + std::to_string(n));
+    auto w = std::make_unique<rh_weight>();
+    w->n = n;
+    w->k = k;
+    w->g = geometry(n, k);
+    const int n_pad = w->g.n_chunks * rh::kBlockN;
+    for (auto& sp : ctx->slots) {
+        Slot& s = *sp;
+        std::lock_guard<std::mutex> lock(s.mu);
+        RH_CUDA(cudaSetDevice(s.device));
+        rh_weight::Per p;
+        p.device = s.device;
+        RH_CUDA(cudaMalloc(&p.q, (size_t)n * (size_t)k));
+        RH_CUDA(cudaMalloc(&p.scales, (size_t)n * sizeof(float)));
+        RH_CUDA(cudaMalloc(&p.tiles, (size_t)w->g.n_chunks * rh::kTileBytes));
+        RH_CUDA(cudaMalloc(&p.colp, (size_t)n_pad * sizeof(float2)));
+        w->per.push_back(p);
+        float* d_w = nullptr;
+        float* d_b = nullptr;
+        RH_CUDA(cudaMalloc(&d_w, (size_t)n * (size_t)k * sizeof(float)));
+        RH_CUDA(cudaMemcpy(d_w, w_nk, (size_t)n * (size_t)k * sizeof(float), cudaMemcpyHostToDevice));
+        if (bias) {
+            RH_CUDA(cudaMalloc(&d_b, (size_t)n * sizeof(float)));
+            RH_CUDA(cudaMemcpy(d_b, bias, (size_t)n * sizeof(float), cudaMemcpyHostToDevice));
+        }
+        rh::PackParams pp{};
+        pp.w = d_w;
+        pp.bias = d_b;
+        pp.n = (int)n;
+        pp.k = (int)k;
+        pp.n_pad = n_pad;
+        pp.merged_tail = w->g.merged;
+        pp.tail_step = w->g.tail_step;
+        pp.q = p.q;
+        pp.scales = p.scales;
+        pp.btiles = p.tiles;
+        pp.colp = p.colp;
+        RH_CUDA(rh::launch_pack(pp, s.stream));
+        s.launches++;
+        RH_CUDA(cudaStreamSynchronize(s.stream));
+        cudaFree(d_w);
+        if (d_b) cudaFree(d_b);
+        if (w->host_scales.empty()) {
+            w->host_scales.resize((size_t)n);
+            RH_CUDA(cudaMemcpy(w->host_scales.data(), p.scales, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost));
+        }
+    }
+    *out = w.release();
+    return RH_OK;
+}
+
+int rh_weight_set_bias(rh_ctx* ctx, rh_weight* w, const float* bias, int64_t bias_len) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (bias && bias_len != w->n)
+        return fail(RH_ERR_INVALID_ARG,
+                    "bias has " + std::to_string(bias_len) + " elements but n is " + std::to_string(w->n));
+    for (auto& s : ctx->slots) s->mu.lock();
+    int rc = upload_colp(w, bias);
+    for (auto& s : ctx->slots) s->mu.unlock();
+    return rc;
+}
+
+int rh_weight_export(rh_ctx* ctx, const rh_weight* w, int8_t* q, float* scales) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w || w->per.empty()) return fail(RH_ERR_INVALID_ARG, "null weight");
+    const auto& p = w->per[0];
+    RH_CUDA(cudaSetDevice(p.device));
+    if (q) RH_CUDA(cudaMemcpy(q, p.q, (size_t)w->n * (size_t)w->k, cudaMemcpyDeviceToHost));
+    if (scales) RH_CUDA(cudaMemcpy(scales, p.scales, (size_t)w->n * sizeof(float), cudaMemcpyDeviceToHost));
+    return RH_OK;
+}
+
+int rh_weight_export_image(rh_ctx* ctx, const rh_weight* w, uint8_t* tiles, float* colp) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w || w->per.empty()) return fail(RH_ERR_INVALID_ARG, "null weight");
+    const auto& p = w->per[0];
+    RH_CUDA(cudaSetDevice(p.device));
+    if (tiles) RH_CUDA(cudaMemcpy(tiles, p.tiles, (size_t)w->g.n_chunks * rh::kTileBytes, cudaMemcpyDeviceToHost));
+    if (colp)
+        RH_CUDA(cudaMemcpy(colp, p.colp, (size_t)w->g.n_chunks * rh::kBlockN * sizeof(float2), cudaMemcpyDeviceToHost));
+    return RH_OK;
+}
+
+int rh_weight_dims(const rh_weight* w, int64_t* n, int64_t* k) {
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (n) *n = w->n;
+    if (k) *k = w->k;
+    return RH_OK;
+}
+
+int64_t rh_weight_device_bytes(const rh_weight* w) {
+    if (!w) return 0;
+    return w->n * w->k + w->n * 4 + (int64_t)w->g.n_chunks * (rh::kTileBytes + rh::kBlockN * 8);
+}
+
+void rh_weight_free(rh_weight* w) {
+    if (!w) return;
+    for (auto& p : w->per) {
+        cudaSetDevice(p.device);
+        cudaDeviceSynchronize();
+        cudaFree(p.q);
+        cudaFree(p.scales);
+        cudaFree(p.tiles);
+        cudaFree(p.colp);
+    }
+    delete w;
+}
+
+int rh_matmul_quantized_b(rh_ctx* ctx, const rh_weight* w, const float* a, int64_t rows, int64_t k, float* out) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (k != w->k)
+        return fail(RH_ERR_INVALID_ARG,
+                    "Inner dimensions must match: " + std::to_string(k) + " != " + std::to_string(w->k));
+    if (rows < 0) return fail(RH_ERR_INVALID_ARG, "negative row count");
+    if (rows == 0) return RH_OK;
+    if (!a || !out) return fail(RH_ERR_INVALID_ARG, "null input or output");
+    return run_host_on_slot(ctx, w, 0, a, rows, nullptr, nullptr, out);
+}
+
+int rh_head_decode(rh_ctx* ctx, const rh_weight* w, const float* a, int64_t rows, int64_t k, int32_t* idx,
+                   float* prob) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (k != w->k)
+        return fail(RH_ERR_INVALID_ARG,
+                    "Inner dimensions must match: " + std::to_string(k) + " != " + std::to_string(w->k));
+    if (rows < 0) return fail(RH_ERR_INVALID_ARG, "negative row count");
+    if (rows == 0) return RH_OK;
+    if (!a || !idx || !prob) return fail(RH_ERR_INVALID_ARG, "null input or output");
+    return run_host_on_slot(ctx, w, 0, a, rows, idx, prob, nullptr);
+}
+
+int rh_head_decode_lines(rh_ctx* ctx, const rh_weight* w, const float* a, const int64_t* line_offsets,
+                         int64_t n_lines, int64_t k, int32_t* idx, float* prob) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (k != w->k)
+        return fail(RH_ERR_INVALID_ARG,
+                    "Inner dimensions must match: " + std::to_string(k) + " != " + std::to_string(w->k));
+    if (n_lines < 0 || (n_lines > 0 && !line_offsets)) return fail(RH_ERR_INVALID_ARG, "bad line offsets");
+    if (n_lines == 0) return RH_OK;
+    if (line_offsets[0] < 0) return fail(RH_ERR_INVALID_ARG, "line offsets must start at >= 0");
+    for (int64_t l = 0; l < n_lines; ++l)
+        if (line_offsets[l + 1] < line_offsets[l]) return fail(RH_ERR_INVALID_ARG, "line offsets must not decrease");
+    const int64_t r0 = line_offsets[0], total = line_offsets[n_lines] - r0;
+    if (total == 0) return RH_OK;
+    if (!a || !idx || !prob) return fail(RH_ERR_INVALID_ARG, "null input or output");
+
+    // Contiguous line shards with balanced timestep counts, one per device.
+    const int nd = (int)ctx->slots.size();
+    std::vector<int64_t> cut(nd + 1, r0);
+    cut[nd] = r0 + total;
+    int64_t l = 0;
+    for (int d = 1; d < nd; ++d) {
+        const int64_t target = r0 + (total * d) / nd;
+        while (l < n_lines && line_offsets[l] < target) ++l;
+        cut[d] = std::max(cut[d - 1], std::min(line_offsets[l], r0 + total));
+    }
+    const std::vector<int> faults = injected_fault_slots();
+    std::vector<int> rc(nd, RH_OK);
+    std::vector<std::string> msg(nd);
+    auto run = [&](int d, int on_slot) {
+        const int64_t rows = cut[d + 1] - cut[d];
+        if (rows <= 0) return;
+        if (std::find(faults.begin(), faults.end(), on_slot) != faults.end()) {
+            rc[d] = RH_ERR_DEVICE_FAULT;
+            msg[d] = "injected failure on slot " + std::to_string(on_slot);
+            return;
+        }
+        rc[d] = run_host_on_slot(ctx, w, on_slot, a + (size_t)(cut[d] - r0) * (size_t)k, rows, idx + (cut[d] - r0),
+                                 prob + (cut[d] - r0), nullptr);
+        if (rc[d]) msg[d] = g_err;
+    };
+    if (nd == 1) {
+        run(0, 0);
+    } else {
+        std::vector<std::thread> th;
+        for (int d = 0; d < nd; ++d) th.emplace_back(run, d, d);
+        for (auto& t : th) t.join();
+    }
+    // Redo failed shards on a healthy device (results do not depend on the device).
+    int healthy = -1;
+    for (int d = 0; d < nd; ++d)
+        if (rc[d] == RH_OK && std::find(faults.begin(), faults.end(), d) == faults.end()) {
+            healthy = d;
+            break;
+        }
+    for (int d = 0; d < nd; ++d) {
+        if (rc[d] == RH_OK) continue;
+        if (rc[d] == RH_ERR_INVALID_ARG) return fail(rc[d], msg[d]);
+        if (healthy < 0) return fail(RH_ERR_DEVICE_FAULT, "every device shard failed; last: " + msg[d]);
+        run(d, healthy);
+        if (rc[d] != RH_OK) return fail(rc[d], msg[d]);
+    }
+    return RH_OK;
+}
+
+int rh_head_decode_device(rh_ctx* ctx, const rh_weight* w, int slot, const float* d_a, int64_t rows, int32_t* d_idx,
+                          float* d_prob, void* stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (slot < 0 || slot >= (int)ctx->slots.size()) return fail(RH_ERR_INVALID_ARG, "slot out of range");
+    if (rows < 0) return fail(RH_ERR_INVALID_ARG, "negative row count");
+    if (rows == 0) return RH_OK;
+    if (!d_a || !d_idx || !d_prob) return fail(RH_ERR_INVALID_ARG, "null device pointer");
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this device");
+    return enqueue_head(ctx, w, s, *pw, d_a, rows, d_idx, d_prob, nullptr, false, (cudaStream_t)stream);
+}
+
+int rh_matmul_quantized_b_device(rh_ctx* ctx, const rh_weight* w, int slot, const float* d_a, int64_t rows,
+                                 float* d_out, void* stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (slot < 0 || slot >= (int)ctx->slots.size()) return fail(RH_ERR_INVALID_ARG, "slot out of range");
+    if (rows < 0) return fail(RH_ERR_INVALID_ARG, "negative row count");
+    if (rows == 0) return RH_OK;
+    if (!d_a || !d_out) return fail(RH_ERR_INVALID_ARG, "null device pointer");
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this device");
+    return enqueue_head(ctx, w, s, *pw, d_a, rows, nullptr, nullptr, d_out, true, (cudaStream_t)stream);
+}
+
+int rh_sync(rh_ctx* ctx, int slot) {
+    if (int rc = check_ctx(ctx)) return rc;
+    int first = slot < 0 ? 0 : slot, last = slot < 0 ? (int)ctx->slots.size() - 1 : slot;
+    if (first < 0 || last >= (int)ctx->slots.size()) return fail(RH_ERR_INVALID_ARG, "slot out of range");
+    int result = RH_OK;
+    for (int i = first; i <= last; ++i) {
+        Slot& s = *ctx->slots[i];
+        std::lock_guard<std::mutex> lock(s.mu);
+        RH_CUDA(cudaSetDevice(s.device));
+        RH_CUDA(cudaDeviceSynchronize());
+        int rc = read_status(s);
+        if (rc && !result) result = rc;
+    }
+    return result;
+}
+
+int64_t rh_launch_count(const rh_ctx* ctx, int slot) {
+    if (!ctx || slot < 0 || slot >= (int)ctx->slots.size()) return -1;
+    return ctx->slots[slot]->launches;
+}
+
+int64_t rh_ctc_collapse(const int32_t* idx, const float* prob, const int64_t* line_offsets, int64_t n_lines,
+                        int32_t* tokens, int64_t* token_offsets, float* scores) {
+    if (n_lines < 0 || !line_offsets || !token_offsets || (n_lines > 0 && !scores)) {
+        g_err = "rh_ctc_collapse: bad arguments";
+        return -1;
+    }
+    for (int64_t l = 0; l < n_lines; ++l)
+        if (line_offsets[l + 1] < line_offsets[l] || line_offsets[l] < 0) {
+            g_err = "rh_ctc_collapse: line offsets must not decrease";
+            return -1;
+        }
+    if (n_lines > 0 && line_offsets[n_lines] > line_offsets[0] && (!idx || !prob || !tokens)) {
+        g_err = "rh_ctc_collapse: null idx/prob/tokens";
+        return -1;
+    }
+    int64_t w = 0;
+    for (int64_t l = 0; l < n_lines; ++l) {
+        token_offsets[l] = w;
+        int32_t last = 0;
+        float sum = 0.0f;
+        int64_t count = 0;
+        for (int64_t t = line_offsets[l]; t < line_offsets[l + 1]; ++t) {
+            const int32_t c = idx[t];
+            if (c != 0 && c != last) {
+                tokens[w++] = c;
+                sum += prob[t];
+                ++count;
+            }
+            last = c;
+        }
+        scores[l] = count == 0 ? 0.0f : sum / (float)count;
+    }
+    token_offsets[n_lines] = w;
+    return w;
+}
+
+}  // extern "C"

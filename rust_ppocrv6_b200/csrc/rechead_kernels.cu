@@ -1,0 +1,574 @@
+// sm_100a kernels of the quantised recognition head (PP-OCRv6 small rec, graph nodes
+// MatMul.12 + Add.204 -> Softmax.2 -> CTC greedy argmax):
+//
+//  pack_kernel   QuantizedWeight::from_f32_transposed (src/ops/matmul.rs:1173-1202) on the
+//                GPU: per-class symmetric int8 + f32 scale, bit-exact; also writes the
+//                tensor-core image of the weight (fp16 tiles in shared-memory order) and the
+//                per-class (scale, bias) epilogue table.
+//  head_kernel   persistent, warp-specialised W8A32 projection. A (f32 features) is split
+//                into two fp16 parts in TMEM, weight tiles stream in through TMA bulk copies,
+//                tcgen05.mma accumulates in TMEM, and the epilogue applies scale + bias and
+//                either
+//                  - FUSED: keeps an online (max, sum exp, first argmax) per row, so only
+//                    idx/prob leave the chip (matmul_quantized_b + softmax_inplace +
+//                    find_argmax, src/ops/matmul.rs:1204, src/ops/softmax.rs:199,
+//                    src/postprocess/ctc.rs:178), or
+//                  - LOGITS: writes the full [m][n] logits (the literal MatMul.12 output).
+//  merge_kernel  combines per-split partial (max, sum, idx) triples when the class range of
+//                a row block was split across CTAs.
+#include <cuda_fp16.h>
+#include <math_constants.h>
+
+#include "head_params.h"
+#include "sm100_ptx.cuh"
+
+namespace rh {
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------- shared memory map
+// (offsets from the 1024-byte aligned base)
+constexpr uint32_t kOffB = 0;                                   // kStages weight tiles
+constexpr uint32_t kOffBars = kStages * kTileBytes;             // mbarriers (32 x 8 B)
+constexpr uint32_t kOffMisc = kOffBars + 32 * 8;                // [0] TMEM base, [1] abort flag
+constexpr uint32_t kOffRho = kOffMisc + 32;                     // [4][128] f32 row de-scale
+constexpr uint32_t kOffQFlag = kOffRho + 4 * 128 * 4;           // [4][4] u32 "quadrant needs de-scale"
+constexpr uint32_t kOffMerge = kOffQFlag + 16 * 4;              // [2][128] float4
+constexpr uint32_t kSmemUsed = kOffMerge + 2 * 128 * 16;
+constexpr uint32_t kSmemBytes = kSmemUsed + 1024;               // + alignment slack
+
+// mbarrier indices
+constexpr int kBarBFull = 0;                     // [kStages] weight tile landed
+constexpr int kBarBEmpty = kBarBFull + kStages;  // [kStages] MMAs reading the tile done
+constexpr int kBarAFull = kBarBEmpty + kStages;  // [2] A operand written to TMEM
+constexpr int kBarAEmpty = kBarAFull + 2;        // [2] MMAs of the unit done with A
+constexpr int kBarAccFull = kBarAEmpty + 2;      // [2] accumulator ready
+constexpr int kBarAccEmpty = kBarAccFull + 2;    // [2] accumulator drained by its epilogue group
+constexpr int kBarRhoFull = kBarAccEmpty + 2;    // [4] per-unit row de-scale written
+constexpr int kBarMFull = kBarRhoFull + 4;       // [2] group-1 partials staged for the merge
+constexpr int kBarMEmpty = kBarMFull + 2;        // [2] group 0 consumed them
+constexpr int kBarMmaDone = kBarMEmpty + 2;      // all MMAs retired (teardown)
+constexpr int kNumBars = kBarMmaDone + 1;
+static_assert(kNumBars <= 32, "barrier area");
+
+// TMEM columns: A operand buffers [0,128) and [128,256), accumulators [256,384), [384,512).
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = 0;
+constexpr uint32_t kTmemAcc = 256;
+
+struct Unit {
+    int mb, sp, c0, c1;
+};
+
+__device__ __forceinline__ Unit unit_of(int u, const HeadParams& p) {
+    Unit U;
+    U.mb = u / p.n_splits;
+    U.sp = u - U.mb * p.n_splits;
+    U.c0 = U.sp * p.chunks_per_split;
+    U.c1 = min(U.c0 + p.chunks_per_split, p.n_chunks);
+    return U;
+}
+
+// Bounded mbarrier wait. Gives up when another role has aborted or after timeout_ns, in
+// which case it raises the CTA abort flag and the device status; every role then leaves
+// its loop and the kernel tears down normally (TMEM freed, copies and MMAs drained).
+__device__ __noinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                      const HeadParams& p, int where) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > p.timeout_ns) {
+            *abort_flag = 1u;
+            atomicOr(p.status, kDevTimeout);
+            atomicExch(p.status + 1, where);
+            return false;
+        }
+    }
+}
+
+// Teardown wait: bounded by time only (used to drain work that is already in flight).
+__device__ __noinline__ void drain_bar(uint32_t bar, uint32_t parity, const HeadParams& p) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > p.timeout_ns) {
+            atomicOr(p.status, kDevTimeout);
+            return;
+        }
+    }
+}
+
+// One fp16 element of the A operand for MMA K-step `step`, slot j (0..15), of a row whose
+// f32 values are `arow` scaled by `rs` (a power of two). Steps [0, hi_steps) hold the high
+// part, steps [hi_steps, hi_steps + lo_steps) the low part; with a merged tail the last
+// high step holds hi(16T..16T+7) in slots 0..7 and lo(16T..16T+7) in slots 8..15 (the
+// weight tile repeats q[16T..16T+7] in the matching K slots).
+__device__ __forceinline__ __half a_part(const float* arow, bool valid, int k, float rs, int step, int j,
+                                         int hi_steps, int merged) {
+    int kk;
+    bool want_lo;
+    if (step < hi_steps) {
+        if (merged && step == hi_steps - 1 && j >= 8) {
+            kk = 16 * step + j - 8;
+            want_lo = true;
+        } else {
+            kk = 16 * step + j;
+            want_lo = false;
+        }
+    } else {
+        kk = 16 * (step - hi_steps) + j;
+        want_lo = true;
+    }
+    if (!valid || kk >= k) return __float2half_rn(0.0f);
+    const float x = __ldg(arow + kk) * rs;
+    const __half h = __float2half_rn(x);
+    if (!want_lo) return h;
+    return __float2half_rn(x - __half2float(h));
+}
+
+template <bool SCALED>
+__device__ __forceinline__ void fused_half(const uint32_t (&v)[64], const float2* __restrict__ cp, int col0,
+                                           float rho, float& run_max, float& run_sum, int& run_idx) {
+    float l[64];
+    float lmax = -CUDART_INF_F;
+#pragma unroll
+    for (int i = 0; i < 64; i += 2) {
+        const float4 sb = __ldg(reinterpret_cast<const float4*>(cp + i));
+        float x0 = __uint_as_float(v[i]);
+        float x1 = __uint_as_float(v[i + 1]);
+        if (SCALED) {
+            x0 *= rho;
+            x1 *= rho;
+        }
+        l[i] = fmaf(x0, sb.x, sb.y);
+        l[i + 1] = fmaf(x1, sb.z, sb.w);
+        lmax = fmaxf(lmax, fmaxf(l[i], l[i + 1]));
+    }
+    if (lmax > run_max) {
+        int first = 63;
+#pragma unroll
+        for (int i = 63; i >= 0; --i)
+            if (l[i] == lmax) first = i;
+        run_sum *= ex2_approx((run_max - lmax) * kLog2e);
+        run_max = lmax;
+        run_idx = col0 + first;
+    }
+    if (run_max == -CUDART_INF_F) return;
+    const float c = -run_max * kLog2e;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; i += 4) {
+        s0 += ex2_approx(fmaf(l[i], kLog2e, c));
+        s1 += ex2_approx(fmaf(l[i + 1], kLog2e, c));
+        s2 += ex2_approx(fmaf(l[i + 2], kLog2e, c));
+        s3 += ex2_approx(fmaf(l[i + 3], kLog2e, c));
+    }
+    run_sum += (s0 + s1) + (s2 + s3);
+}
+
+template <bool SCALED>
+__device__ __forceinline__ void logits_half(const uint32_t (&v)[64], const float2* __restrict__ cp, int col0,
+                                            float rho, float* __restrict__ out_row, int n) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+        const float2 sb = __ldg(cp + i);
+        float x = __uint_as_float(v[i]);
+        if (SCALED) x *= rho;
+        if (col0 + i < n) out_row[col0 + i] = fmaf(x, sb.x, sb.y);
+    }
+}
+
+// Merges two (max, sum of exp(l - max), first argmax) triples; ties keep the lower class.
+__device__ __forceinline__ void combine(float& m0, float& s0, int& i0, float m1, float s1, int i1) {
+    const bool take1 = (m1 > m0) || (m1 == m0 && i1 < i0);
+    const float M = take1 ? m1 : m0;
+    float S = 0.f;
+    if (m0 != -CUDART_INF_F) S += s0 * ex2_approx((m0 - M) * kLog2e);
+    if (m1 != -CUDART_INF_F) S += s1 * ex2_approx((m1 - M) * kLog2e);
+    i0 = take1 ? i1 : i0;
+    m0 = M;
+    s0 = S;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------- pack
+// One warp per (padded) class row. Lane l holds K values l, l+32, l+64, l+96.
+__global__ void __launch_bounds__(256) pack_kernel(const PackParams p) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= p.n_pad) return;
+    const int j = warp;
+    const bool real = j < p.n;
+    float w[4];
+    float max_abs = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int kk = lane + 32 * i;
+        w[i] = (real && kk < p.k) ? p.w[(size_t)j * p.k + kk] : 0.0f;
+        max_abs = fmaxf(max_abs, fabsf(w[i]));  // fmaxf ignores NaN, like f32::max
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) max_abs = fmaxf(max_abs, __shfl_xor_sync(0xffffffffu, max_abs, o));
+    const float scale = max_abs > 1e-8f ? max_abs / 127.0f : 1.0f;  // IEEE division (no fast-math)
+    const float inv_scale = 1.0f / scale;
+    int q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float v = roundf(w[i] * inv_scale);  // half away from zero, like f32::round
+        int qi;
+        if (isnan(v))
+            qi = 0;  // `NaN as i8` == 0
+        else
+            qi = (int)fminf(fmaxf(v, -127.0f), 127.0f);
+        q[i] = real ? qi : 0;
+        const int kk = lane + 32 * i;
+        if (real && kk < p.k) p.q[(size_t)j * p.k + kk] = (int8_t)qi;
+    }
+    if (real && lane == 0) p.scales[j] = scale;
+    if (lane == 0) p.colp[j] = real ? make_float2(scale, p.bias ? p.bias[j] : 0.0f) : make_float2(0.0f, -CUDART_INF_F);
+
+    // tensor-core image: tile j/128, row r = j%128, K slot s -> byte offset
+    // (s/64)*16384 + r*128 + (((s%64)/8) ^ (r%8))*16 + (s%8)*2
+    const int tile = j >> 7, r = j & 127;
+    uint8_t* img = p.btiles + (size_t)tile * kTileBytes;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int s = lane * 4 + t;  // K slot 0..127
+        int src = s;
+        if (p.merged_tail && s >= 16 * p.tail_step + 8 && s < 16 * p.tail_step + 16) src = s - 8;
+        const bool ok = src < p.k;
+        const int from = src & 31, reg = src >> 5;
+        const int v0 = __shfl_sync(0xffffffffu, q[0], from);
+        const int v1 = __shfl_sync(0xffffffffu, q[1], from);
+        const int v2 = __shfl_sync(0xffffffffu, q[2], from);
+        const int v3 = __shfl_sync(0xffffffffu, q[3], from);
+        const int val = reg == 0 ? v0 : reg == 1 ? v1 : reg == 2 ? v2 : v3;
+        const __half h = __int2half_rn(ok ? val : 0);
+        const uint32_t off = (uint32_t)(s >> 6) * 16384u + (uint32_t)r * 128u +
+                             (uint32_t)((((s & 63) >> 3) ^ (r & 7)) << 4) + (uint32_t)(s & 7) * 2u;
+        *reinterpret_cast<__half*>(img + off) = h;
+    }
+}
+
+// -------------------------------------------------------------------- head
+// Warp roles (one CTA per SM, persistent over work units = (row block, class range)):
+//   warp 0      lane 0: weight-tile producer (TMA bulk copies into the smem ring)
+//   warp 1      TMEM allocator; lane 0: MMA issuer
+//   warps 2-3   idle
+//   warps 4-7   A converters: f32 rows -> (hi, lo) fp16 parts in TMEM, one lane quadrant each
+//   warps 8-11  epilogue group 0 (accumulator buffer 0), lane quadrants 0-3
+//   warps 12-15 epilogue group 1 (accumulator buffer 1)
+template <bool EMIT_LOGITS>
+__global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_constant__ HeadParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    const uint32_t base = (raw_u32 + 1023u) & ~1023u;
+    uint8_t* gbase = smem_raw + (base - raw_u32);
+    uint32_t* misc = reinterpret_cast<uint32_t*>(gbase + kOffMisc);
+    volatile uint32_t* abort_flag = misc + 1;
+    float* rho_s = reinterpret_cast<float*>(gbase + kOffRho);
+    uint32_t* qflag_s = reinterpret_cast<uint32_t*>(gbase + kOffQFlag);
+    float4* merge_s = reinterpret_cast<float4*>(gbase + kOffMerge);
+    auto bar = [&](int i) -> uint32_t { return base + kOffBars + 8u * (uint32_t)i; };
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int units = p.n_mblocks * p.n_splits;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(bar(kBarBFull + s), 1);
+            mbar_init(bar(kBarBEmpty + s), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar(kBarAFull + i), 128);
+            mbar_init(bar(kBarAEmpty + i), 1);
+            mbar_init(bar(kBarAccFull + i), 1);
+            mbar_init(bar(kBarAccEmpty + i), 128);
+            mbar_init(bar(kBarMFull + i), 128);
+            mbar_init(bar(kBarMEmpty + i), 128);
+        }
+        for (int i = 0; i < 4; ++i) mbar_init(bar(kBarRhoFull + i), 128);
+        mbar_init(bar(kBarMmaDone), 1);
+        misc[1] = 0u;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(base + kOffMisc, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = misc[0];
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            uint32_t cc = 0, issued = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+                const Unit U = unit_of(u, p);
+                for (int c = U.c0; c < U.c1; ++c, ++cc) {
+                    const int s = (int)(cc % kStages);
+                    if (!wait_bar(bar(kBarBEmpty + s), ((cc / kStages) & 1u) ^ 1u, abort_flag, p, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    if (p.debug_flags & kDebugStallProducer) continue;
+                    mbar_arrive_expect_tx(bar(kBarBFull + s), kTileBytes);
+                    bulk_copy_g2s(base + kOffB + (uint32_t)s * kTileBytes, p.btiles + (size_t)c * kTileBytes,
+                                  kTileBytes, bar(kBarBFull + s));
+                    issued = cc + 1;
+                }
+            }
+            // Drain: the last copy issued into each stage must land before the CTA exits.
+            for (uint32_t s = 0; s < (uint32_t)kStages && s < issued; ++s) {
+                const uint32_t fills = (issued - 1 - s) / kStages + 1;
+                drain_bar(bar(kBarBFull + (int)s), (fills - 1) & 1u, p);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(128, 128);
+            const int steps = p.hi_steps + p.lo_steps;
+            uint32_t cc = 0, uc = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
+                const Unit U = unit_of(u, p);
+                const uint32_t ab = uc & 1u;
+                if (!wait_bar(bar(kBarAFull + ab), (uc >> 1) & 1u, abort_flag, p, 2)) break;
+                tc_fence_after();
+                const uint32_t a_tmem = tmem + kTmemA + ab * 128u;
+                for (int c = U.c0; c < U.c1; ++c, ++cc) {
+                    const int s = (int)(cc % kStages);
+                    const uint32_t buf = cc & 1u;
+                    if (!wait_bar(bar(kBarBFull + s), (cc / kStages) & 1u, abort_flag, p, 3) ||
+                        !wait_bar(bar(kBarAccEmpty + buf), ((cc >> 1) & 1u) ^ 1u, abort_flag, p, 4)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem + kTmemAcc + buf * 128u;
+                    const uint32_t b_smem = base + kOffB + (uint32_t)s * kTileBytes;
+                    for (int step = 0; step < steps; ++step) {
+                        const int kc = step < p.hi_steps ? step : step - p.hi_steps;
+                        const uint64_t bdesc =
+                            smem_desc_k_sw128(b_smem + (uint32_t)(kc >> 2) * 16384u + (uint32_t)(kc & 3) * 32u);
+                        mma_f16_ts(d_tmem, a_tmem + (uint32_t)step * 8u, bdesc, idesc, step > 0 ? 1u : 0u);
+                    }
+                    mma_commit(bar(kBarBEmpty + s));
+                    mma_commit(bar(kBarAccFull + (int)buf));
+                }
+                if (!ok) break;
+                mma_commit(bar(kBarAEmpty + (int)ab));
+            }
+            mma_commit(bar(kBarMmaDone));
+            drain_bar(bar(kBarMmaDone), 0u, p);
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ----------------------------------------------------------- converters
+        const int q = warp & 3;
+        const int r = q * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        const int steps = p.hi_steps + p.lo_steps;
+        uint32_t uc = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc) {
+            const Unit U = unit_of(u, p);
+            const uint32_t ab = uc & 1u, slot = uc & 3u;
+            if (!wait_bar(bar(kBarAEmpty + (int)ab), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 5)) break;
+            tc_fence_after();
+            const long long row = (long long)U.mb * kBlockM + r;
+            const bool valid = row < p.m;
+            const float* arow = p.a + (valid ? row : 0) * (long long)p.k;
+            float max_abs = 0.0f;
+            if (valid)
+                for (int kk = 0; kk < p.k; ++kk) max_abs = fmaxf(max_abs, fabsf(__ldg(arow + kk)));
+            // fp16 holds the parts only below 65504: rows with max|a| >= 2^14 are scaled by a
+            // power of two (exact) into [2^14, 2^15) and de-scaled in the epilogue.
+            float rs = 1.0f, rho = 1.0f;
+            if (max_abs >= 16384.0f && max_abs <= 3.4028235e38f) {
+                const int e = (int)((__float_as_uint(max_abs) >> 23) & 0xFFu) - 127;
+                rs = __uint_as_float((uint32_t)(127 + 14 - e) << 23);
+                rho = __uint_as_float((uint32_t)(127 + e - 14) << 23);
+            }
+            const uint32_t need = __ballot_sync(0xffffffffu, rs != 1.0f);
+            for (int g4 = 0; g4 * 4 < steps; ++g4) {
+                uint32_t wv[32];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int step = g4 * 4 + t;
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) {
+                        uint32_t packed = 0u;
+                        if (step < steps) {
+                            const __half lo_h = a_part(arow, valid, p.k, rs, step, 2 * w, p.hi_steps, p.merged_tail);
+                            const __half hi_h =
+                                a_part(arow, valid, p.k, rs, step, 2 * w + 1, p.hi_steps, p.merged_tail);
+                            packed = (uint32_t)__half_as_ushort(lo_h) | ((uint32_t)__half_as_ushort(hi_h) << 16);
+                        }
+                        wv[t * 8 + w] = packed;
+                    }
+                }
+                tmem_st32x32b_x32(tmem + lane_base + kTmemA + ab * 128u + (uint32_t)g4 * 32u, wv);
+            }
+            tmem_st_wait();
+            rho_s[slot * 128 + r] = rho;
+            if (lane == 0) qflag_s[slot * 4 + q] = need;
+            tc_fence_before();
+            mbar_arrive(bar(kBarAFull + (int)ab));
+            mbar_arrive(bar(kBarRhoFull + (int)slot));
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------------------- epilogue
+        const int g = (warp - 8) >> 2;
+        const int q = warp & 3;
+        const int r = q * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        uint32_t cc = 0, uc = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
+            const Unit U = unit_of(u, p);
+            const uint32_t slot = uc & 3u;
+            const long long row = (long long)U.mb * kBlockM + r;
+            float run_max = -CUDART_INF_F, run_sum = 0.0f;
+            int run_idx = 0;
+            bool have_rho = false, scaled = false;
+            float rho = 1.0f;
+            for (int c = U.c0; c < U.c1; ++c, ++cc) {
+                const uint32_t buf = cc & 1u;
+                if ((int)buf != g) continue;
+                if (!have_rho) {
+                    if (!wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6)) {
+                        ok = false;
+                        break;
+                    }
+                    rho = rho_s[slot * 128 + r];
+                    scaled = qflag_s[slot * 4 + q] != 0u;
+                    have_rho = true;
+                }
+                if (!wait_bar(bar(kBarAccFull + (int)buf), (cc >> 1) & 1u, abort_flag, p, 7)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem + lane_base + kTmemAcc + buf * 128u;
+                const float2* cp = p.colp + (size_t)c * kBlockN;
+                const int col0 = c * kBlockN;
+                uint32_t v[64];
+                tmem_ld32x32b_x64_wait(taddr, v);
+                if (EMIT_LOGITS) {
+                    float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
+                    if (row < p.m) {
+                        if (scaled) logits_half<true>(v, cp, col0, rho, out_row, p.n);
+                        else logits_half<false>(v, cp, col0, rho, out_row, p.n);
+                    }
+                } else {
+                    if (scaled) fused_half<true>(v, cp, col0, rho, run_max, run_sum, run_idx);
+                    else fused_half<false>(v, cp, col0, rho, run_max, run_sum, run_idx);
+                }
+                tmem_ld32x32b_x64_wait(taddr + 64u, v);
+                tc_fence_before();
+                mbar_arrive(bar(kBarAccEmpty + (int)buf));
+                if (EMIT_LOGITS) {
+                    float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
+                    if (row < p.m) {
+                        if (scaled) logits_half<true>(v, cp + 64, col0 + 64, rho, out_row, p.n);
+                        else logits_half<false>(v, cp + 64, col0 + 64, rho, out_row, p.n);
+                    }
+                } else {
+                    if (scaled) fused_half<true>(v, cp + 64, col0 + 64, rho, run_max, run_sum, run_idx);
+                    else fused_half<false>(v, cp + 64, col0 + 64, rho, run_max, run_sum, run_idx);
+                }
+            }
+            if (!ok) break;
+            if (!EMIT_LOGITS) {
+                // Merge the two groups' partial rows for this unit through shared memory.
+                const uint32_t mb2 = uc & 1u;
+                float4* mg = merge_s + mb2 * 128;
+                if (g == 1) {
+                    if (!wait_bar(bar(kBarMEmpty + (int)mb2), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 8)) break;
+                    mg[r] = make_float4(run_max, run_sum, __int_as_float(run_idx), 0.0f);
+                    mbar_arrive(bar(kBarMFull + (int)mb2));
+                } else {
+                    if (!wait_bar(bar(kBarMFull + (int)mb2), (uc >> 1) & 1u, abort_flag, p, 9)) break;
+                    const float4 o = mg[r];
+                    mbar_arrive(bar(kBarMEmpty + (int)mb2));
+                    combine(run_max, run_sum, run_idx, o.x, o.y, __float_as_int(o.z));
+                    if (row < p.m) {
+                        if (p.n_splits == 1) {
+                            p.idx[row] = run_idx;
+                            p.prob[row] = 1.0f / run_sum;
+                        } else {
+                            p.partial[(size_t)U.sp * (size_t)p.m + (size_t)row] =
+                                make_float4(run_max, run_sum, __int_as_float(run_idx), 0.0f);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------- merge
+__global__ void __launch_bounds__(256) merge_kernel(const float4* __restrict__ partial, int n_splits, long long m,
+                                                    int32_t* __restrict__ idx, float* __restrict__ prob) {
+    const long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= m) return;
+    float M = -CUDART_INF_F, S = 0.0f;
+    int I = 0;
+    for (int s = 0; s < n_splits; ++s) {
+        const float4 v = partial[(size_t)s * (size_t)m + (size_t)row];
+        combine(M, S, I, v.x, v.y, __float_as_int(v.z));
+    }
+    idx[row] = I;
+    prob[row] = 1.0f / S;
+}
+
+// ------------------------------------------------------------------ launchers
+size_t head_smem_bytes() { return kSmemBytes; }
+
+cudaError_t head_kernel_setup() {
+    cudaError_t e = cudaFuncSetAttribute(head_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(head_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+}
+
+cudaError_t launch_pack(const PackParams& p, cudaStream_t stream) {
+    const int threads = 256;
+    const long long total = (long long)p.n_pad * 32;
+    const int blocks = (int)((total + threads - 1) / threads);
+    pack_kernel<<<blocks, threads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_head(const HeadParams& p, bool emit_logits, int grid, cudaStream_t stream) {
+    if (emit_logits)
+        head_kernel<true><<<grid, kHeadThreads, kSmemBytes, stream>>>(p);
+    else
+        head_kernel<false><<<grid, kHeadThreads, kSmemBytes, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge(const float4* partial, int n_splits, long long m, int32_t* idx, float* prob,
+                         cudaStream_t stream) {
+    const int threads = 256;
+    const int blocks = (int)((m + threads - 1) / threads);
+    merge_kernel<<<blocks, threads, 0, stream>>>(partial, n_splits, m, idx, prob);
+    return cudaGetLastError();
+}
+
+}  // namespace rh
