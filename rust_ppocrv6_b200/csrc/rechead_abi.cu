@@ -185,9 +185,11 @@ int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per&
 
 int read_status(Slot& s) {
     int st[2] = {0, 0};
-    RH_CUDA(cudaMemcpy(st, s.d_status, sizeof(st), cudaMemcpyDeviceToHost));
+    RH_CUDA(cudaMemcpyAsync(st, s.d_status, sizeof(st), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaStreamSynchronize(s.stream));
     if (st[0] != 0) {
-        RH_CUDA(cudaMemset(s.d_status, 0, 2 * sizeof(int)));
+        RH_CUDA(cudaMemsetAsync(s.d_status, 0, 2 * sizeof(int), s.stream));
+        RH_CUDA(cudaStreamSynchronize(s.stream));
         if (st[0] & rh::kDevTimeout)
             return fail(RH_ERR_TIMEOUT, "device wait timed out (site " + std::to_string(st[1]) +
                                             "); the kernel gave up and the context is still usable");
@@ -235,7 +237,7 @@ int run_host_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, 
     return read_status(s);
 }
 
-int upload_colp(rh_weight* w, const float* bias) {
+int upload_colp(rh_ctx* ctx, rh_weight* w, const float* bias) {
     const int n_pad = w->g.n_chunks * rh::kBlockN;
     std::vector<float2> colp(n_pad);
     for (int j = 0; j < n_pad; ++j) {
@@ -245,8 +247,15 @@ int upload_colp(rh_weight* w, const float* bias) {
             colp[j] = make_float2(0.0f, -INFINITY);
     }
     for (auto& p : w->per) {
+        Slot* slot = nullptr;
+        for (auto& sp : ctx->slots)
+            if (sp->device == p.device) slot = sp.get();
+        if (!slot) return fail(RH_ERR_INVALID_ARG, "weight device is not in this context");
         RH_CUDA(cudaSetDevice(p.device));
-        RH_CUDA(cudaMemcpy(p.colp, colp.data(), colp.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        // ordered after every kernel already queued on the slot stream that reads the table
+        RH_CUDA(cudaMemcpyAsync(p.colp, colp.data(), colp.size() * sizeof(float2), cudaMemcpyHostToDevice,
+                                slot->stream));
+        RH_CUDA(cudaStreamSynchronize(slot->stream));
     }
     return RH_OK;
 }
@@ -298,7 +307,8 @@ int rh_ctx_create(const int* devices, int n_devices, rh_ctx** out) {
         RH_CUDA(rh::head_kernel_setup());
         RH_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
         RH_CUDA(cudaMalloc(&s->d_status, 2 * sizeof(int)));
-        RH_CUDA(cudaMemset(s->d_status, 0, 2 * sizeof(int)));
+        RH_CUDA(cudaMemsetAsync(s->d_status, 0, 2 * sizeof(int), s->stream));
+        RH_CUDA(cudaStreamSynchronize(s->stream));
         ctx->slots.push_back(std::move(s));
     }
     *out = ctx.release();
@@ -361,10 +371,12 @@ int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const f
         float* d_w = nullptr;
         float* d_b = nullptr;
         RH_CUDA(cudaMalloc(&d_w, (size_t)n * (size_t)k * sizeof(float)));
-        RH_CUDA(cudaMemcpy(d_w, w_nk, (size_t)n * (size_t)k * sizeof(float), cudaMemcpyHostToDevice));
+        // Stream-ordered copies: a plain cudaMemcpy from pageable memory may return before its
+        // DMA lands, and the pack kernel runs on a non-blocking stream.
+        RH_CUDA(cudaMemcpyAsync(d_w, w_nk, (size_t)n * (size_t)k * sizeof(float), cudaMemcpyHostToDevice, s.stream));
         if (bias) {
             RH_CUDA(cudaMalloc(&d_b, (size_t)n * sizeof(float)));
-            RH_CUDA(cudaMemcpy(d_b, bias, (size_t)n * sizeof(float), cudaMemcpyHostToDevice));
+            RH_CUDA(cudaMemcpyAsync(d_b, bias, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, s.stream));
         }
         rh::PackParams pp{};
         pp.w = d_w;
@@ -385,7 +397,9 @@ int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const f
         if (d_b) cudaFree(d_b);
         if (w->host_scales.empty()) {
             w->host_scales.resize((size_t)n);
-            RH_CUDA(cudaMemcpy(w->host_scales.data(), p.scales, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost));
+            RH_CUDA(cudaMemcpyAsync(w->host_scales.data(), p.scales, (size_t)n * sizeof(float),
+                                    cudaMemcpyDeviceToHost, s.stream));
+            RH_CUDA(cudaStreamSynchronize(s.stream));
         }
     }
     *out = w.release();
@@ -399,7 +413,7 @@ int rh_weight_set_bias(rh_ctx* ctx, rh_weight* w, const float* bias, int64_t bia
         return fail(RH_ERR_INVALID_ARG,
                     "bias has " + std::to_string(bias_len) + " elements but n is " + std::to_string(w->n));
     for (auto& s : ctx->slots) s->mu.lock();
-    int rc = upload_colp(w, bias);
+    int rc = upload_colp(ctx, w, bias);
     for (auto& s : ctx->slots) s->mu.unlock();
     return rc;
 }
@@ -409,6 +423,7 @@ int rh_weight_export(rh_ctx* ctx, const rh_weight* w, int8_t* q, float* scales) 
     if (!w || w->per.empty()) return fail(RH_ERR_INVALID_ARG, "null weight");
     const auto& p = w->per[0];
     RH_CUDA(cudaSetDevice(p.device));
+    RH_CUDA(cudaDeviceSynchronize());
     if (q) RH_CUDA(cudaMemcpy(q, p.q, (size_t)w->n * (size_t)w->k, cudaMemcpyDeviceToHost));
     if (scales) RH_CUDA(cudaMemcpy(scales, p.scales, (size_t)w->n * sizeof(float), cudaMemcpyDeviceToHost));
     return RH_OK;
@@ -419,6 +434,7 @@ int rh_weight_export_image(rh_ctx* ctx, const rh_weight* w, uint8_t* tiles, floa
     if (!w || w->per.empty()) return fail(RH_ERR_INVALID_ARG, "null weight");
     const auto& p = w->per[0];
     RH_CUDA(cudaSetDevice(p.device));
+    RH_CUDA(cudaDeviceSynchronize());
     if (tiles) RH_CUDA(cudaMemcpy(tiles, p.tiles, (size_t)w->g.n_chunks * rh::kTileBytes, cudaMemcpyDeviceToHost));
     if (colp)
         RH_CUDA(cudaMemcpy(colp, p.colp, (size_t)w->g.n_chunks * rh::kBlockN * sizeof(float2), cudaMemcpyDeviceToHost));

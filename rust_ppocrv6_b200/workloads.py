@@ -68,18 +68,38 @@ def dequantized(w_t: np.ndarray):
 
 def make_near_ties(rng, x: np.ndarray, rows: np.ndarray, w_deq: np.ndarray, bias: np.ndarray) -> None:
     """Rewrites x[rows] so that two chosen classes are the top-2 logits with a gap in
-    [1e-6, 1e-4) (on the quantised weights, in f64 before the f32 rounding of x)."""
-    n = w_deq.shape[0]
+    [1e-6, 1e-4) (on the quantised weights, in f64 before the f32 rounding of x).
+
+    The two classes come from the highest-norm tenth of the vocabulary; x is the least-norm
+    solution of w1.x = L - b1, w2.x = L - b2 - gap plus a little noise orthogonal to both,
+    and the construction is verified (top-2 are the chosen classes, third logit at least
+    0.5 below), else retried with another pair and a larger L."""
+    n, k = w_deq.shape
     b = bias.astype(np.float64)
+    norms = np.linalg.norm(w_deq, axis=1)
+    strong = np.argsort(norms)[-max(2, n // 10):]
     for r in rows:
-        c1, c2 = rng.choice(n, size=2, replace=False)
-        v = w_deq[c1] + w_deq[c2]
-        xr = 0.3 * rng.standard_normal(x.shape[1]) + 6.0 * v / max(np.dot(v, v), 1e-12) ** 0.5
-        g = w_deq[c1] - w_deq[c2]
-        gap = rng.uniform(1e-6, 1e-4)
-        d = np.dot(g, xr) + b[c1] - b[c2]
-        xr = xr - (d - gap) * g / max(np.dot(g, g), 1e-30)
-        x[r] = xr.astype(np.float32)
+        target = 4.0
+        for attempt in range(64):
+            c1, c2 = rng.choice(strong, size=2, replace=False)
+            W = np.stack([w_deq[c1], w_deq[c2]])
+            gap = rng.uniform(1e-6, 1e-4)
+            rhs = np.array([target - b[c1], target - gap - b[c2]])
+            gram = W @ W.T
+            if abs(np.linalg.det(gram)) < 1e-12:
+                continue
+            xr = W.T @ np.linalg.solve(gram, rhs)
+            noise = 0.2 * rng.standard_normal(k)
+            noise -= W.T @ np.linalg.solve(gram, W @ noise)  # keep both target logits exact
+            xr = xr + noise
+            logits = w_deq @ xr + b
+            order = np.argsort(logits)[::-1]
+            if {order[0], order[1]} == {c1, c2} and logits[order[2]] < logits[order[1]] - 0.5:
+                x[r] = xr.astype(np.float32)
+                break
+            target *= 1.15
+        else:
+            raise RuntimeError("could not build a near-tie row")
 
 
 def make(cfg: int, scale: float = 1.0, seed: int = SEED) -> Workload:

@@ -131,6 +131,21 @@ def test_tensor_core_image_layout(rh, ctx, oracle, n, k):
     assert np.array_equal(colp, cp)
 
 
+def test_pack_is_stream_ordered_with_pageable_input(rh, ctx, oracle):
+    """Regression: the weight upload must be ordered before the pack kernel on the context's
+    non-blocking stream (a plain cudaMemcpy from pageable memory may return before its DMA
+    lands). Repacks a 6906 x 80 weight (the tiny-model head shape) and checks every image."""
+    rng = np.random.default_rng(6906)
+    w = (0.05 * rng.standard_normal((6906, 80))).astype(np.float32)
+    q, s = oracle.pack(w)
+    img, cp = expected_image(q, s, None, 80)
+    for _ in range(12):
+        qw = rh.QuantizedWeight.from_f32_transposed(w.copy(), ctx=ctx)
+        tiles, colp = qw.tensor_core_image()
+        assert np.array_equal(tiles, img) and np.array_equal(colp, cp)
+        qw.free()
+
+
 # ---------------------------------------------------------------- logits
 
 
