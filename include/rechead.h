@@ -133,6 +133,30 @@ int rh_head_decode_device(rh_ctx *ctx, const rh_weight *w, int slot, const float
 int rh_matmul_quantized_b_device(rh_ctx *ctx, const rh_weight *w, int slot, const float *d_a, int64_t rows,
                                  float *d_out, void *stream);
 
+/*
+ * rh_head_decode_device with no memory allocation. No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory while they run — a host that
+ * reserves all GPU memory up front for its own allocator, or a latency-critical loop that
+ * must not call cudaMalloc/cudaFree because both synchronise the device.
+ * Its only scratch (the per-split partial rows that the class-range split writes and the
+ * merge kernel reads) is a fixed 4 MiB array in the library's device image, so every GPU that
+ * uses the library holds those 4 MiB until the process exits. Limit: at most 262,144
+ * timestep rows per call (larger calls fail with RH_ERR_INVALID_ARG and launch nothing);
+ * the class-range split is coarsened when splits x rows would not fit.
+ *  - The first call on a device resolves the array's device address (cudaGetSymbolAddress,
+ *    which may load the library's device code); make that first call before any stream
+ *    capture.
+ *  - Every call on a device shares the one array and no part of it has to start at zero (the
+ *    head kernel writes every entry the merge kernel reads), but calls whose work overlaps on
+ *    the GPU (different streams, or different contexts on the same device) race on it: order
+ *    them on one stream or with events.
+ *  - Calls no cudaMalloc, cudaFree or other allocating routine; the context and the packed
+ *    weight are created beforehand. Failures surface at rh_sync(), as for the other
+ *    "_device" forms.
+ */
+int rh_head_decode_device_noalloc(rh_ctx *ctx, const rh_weight *w, int slot, const float *d_a, int64_t rows,
+                                  int32_t *d_idx, float *d_prob, void *stream);
+
 /* Waits for all work on device `slot` (slot < 0: every device) and reports device-side
  * failures (RH_ERR_TIMEOUT) recorded since the previous rh_sync. */
 int rh_sync(rh_ctx *ctx, int slot);

@@ -260,6 +260,35 @@ int upload_colp(rh_ctx* ctx, rh_weight* w, const float* bias) {
     return RH_OK;
 }
 
+// ----------------------------------------------------------- no-allocation entry point
+// Some callers cannot allocate device memory at run time: a host that pre-reserves all GPU
+// memory for itself, code that must not call cudaMalloc/cudaFree inside a latency-critical
+// loop (both synchronise the device), or an embedder with its own allocator that forbids
+// foreign allocations. rh_head_decode_device_noalloc serves them: its only scratch (the
+// per-split partial (max, sum, argmax) rows that the class-range split writes and the merge
+// kernel reads) lives in this fixed file-scope device array.
+constexpr int64_t kNoAllocScratchEntries = 262144;  // float4 entries: 4 MiB per GPU
+static __device__ __align__(256) float4 g_noalloc_scratch[kNoAllocScratchEntries];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[256] = {};  // device address of g_noalloc_scratch, per device ordinal
+
+// Set-up, once per device, with that device current: the array's name is only a host-side
+// stand-in, so the device address comes from cudaGetSymbolAddress.
+int noalloc_scratch(int device, float4** out) {
+    if (device < 0 || device >= 256) return fail(RH_ERR_UNSUPPORTED, "device ordinal above 255");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr)
+            return fail(RH_ERR_CUDA, std::string("cudaGetSymbolAddress(g_noalloc_scratch): ") + cudaGetErrorString(e));
+        g_noalloc_ptr[device] = ptr;
+    }
+    *out = static_cast<float4*>(g_noalloc_ptr[device]);
+    return RH_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -643,6 +672,65 @@ int64_t rh_ctc_collapse(const int32_t* idx, const float* prob, const int64_t* li
     }
     token_offsets[n_lines] = w;
     return w;
+}
+
+
+int rh_head_decode_device_noalloc(rh_ctx* ctx, const rh_weight* w, int slot, const float* d_a, int64_t rows,
+                                  int32_t* d_idx, float* d_prob, void* stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (slot < 0 || slot >= (int)ctx->slots.size()) return fail(RH_ERR_INVALID_ARG, "slot out of range");
+    if (rows < 0) return fail(RH_ERR_INVALID_ARG, "negative row count");
+    if (rows > kNoAllocScratchEntries)
+        return fail(RH_ERR_INVALID_ARG, "rh_head_decode_device_noalloc: " + std::to_string(rows) +
+                                            " rows exceed its static limit of " +
+                                            std::to_string(kNoAllocScratchEntries) +
+                                            " timestep rows per call; split the batch or use rh_head_decode_device");
+    if (rows == 0) return RH_OK;
+    if (!d_a || !d_idx || !d_prob) return fail(RH_ERR_INVALID_ARG, "null device pointer");
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this device");
+    float4* scratch = nullptr;
+    if (int rc = noalloc_scratch(s.device, &scratch)) return rc;
+
+    int n_mblocks, n_splits, cps, grid;
+    plan(rows, w->g.n_chunks, s.sms, n_mblocks, n_splits, cps, grid);
+    if (n_splits > 1 && (int64_t)n_splits * rows > kNoAllocScratchEntries) {
+        // fewer, longer class ranges so that splits x rows partial entries fit the array
+        const int max_splits = (int)(kNoAllocScratchEntries / rows);
+        cps = max_splits <= 1 ? w->g.n_chunks : (w->g.n_chunks + max_splits - 1) / max_splits;
+        n_splits = (w->g.n_chunks + cps - 1) / cps;
+        grid = (int)std::min<long long>((long long)n_mblocks * n_splits, s.sms);
+    }
+    rh::HeadParams p{};
+    p.a = d_a;
+    p.m = rows;
+    p.k = (int)w->k;
+    p.n = (int)w->n;
+    p.n_chunks = w->g.n_chunks;
+    p.hi_steps = w->g.hi_steps;
+    p.lo_steps = w->g.lo_steps;
+    p.merged_tail = w->g.merged;
+    p.btiles = pw->tiles;
+    p.colp = pw->colp;
+    p.n_mblocks = n_mblocks;
+    p.n_splits = n_splits;
+    p.chunks_per_split = cps;
+    p.idx = d_idx;
+    p.prob = d_prob;
+    p.partial = n_splits > 1 ? scratch : nullptr;
+    p.status = s.d_status;
+    p.timeout_ns = ctx->timeout_ns;
+    RH_CUDA(rh::launch_head(p, false, grid, (cudaStream_t)stream));
+    s.launches++;
+    if (n_splits > 1) {
+        RH_CUDA(rh::launch_merge(scratch, n_splits, rows, d_idx, d_prob, (cudaStream_t)stream));
+        s.launches++;
+    }
+    return RH_OK;
 }
 
 }  // extern "C"
