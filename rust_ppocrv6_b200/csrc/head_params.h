@@ -11,13 +11,14 @@ constexpr int kBlockN = 128;                  // classes per weight tile / accum
 constexpr int kPadK = 128;                    // K extent of a weight tile (K <= 128 supported)
 constexpr int kTileBytes = kBlockN * kPadK * 2;  // one fp16 weight tile: 32 KB
 constexpr int kStages = 4;                    // weight-tile ring depth in shared memory
-constexpr int kHeadThreads = 512;             // 16 warps, see head_kernel
+constexpr int kHeadThreads = 768;             // 24 warps, see head_kernel
 
 // Device status word bits (status[0]); status[1] records which wait gave up.
 constexpr int kDevTimeout = 1;
 // Test-only: the weight producer never fills its stages, so every consumer's bounded wait
 // runs out and the kernel must return kDevTimeout with the context intact.
 constexpr int kDebugStallProducer = 1;
+constexpr int kDefaultPolyPairs = 4;
 
 struct HeadParams {
     const float* a;            // [m][k] timestep features (rows packed densely)
@@ -30,16 +31,18 @@ struct HeadParams {
     int merged_tail;           // 1: hi step hi_steps-1 also carries lo's last 8 K values
     const uint8_t* btiles;     // n_chunks * 32 KB, fp16 weight tiles in the smem image order
     const float2* colp;        // n_chunks * 128 (scale, bias); padded columns (0, -inf)
+    const float* ctab;         // n_chunks * 256: per tile c[128] = scale*log2(e), e[128] = bias*log2(e)
     int n_mblocks;             // ceil(m / 128)
     int n_splits;              // class-range splits per row block
     int chunks_per_split;
     int32_t* idx;              // fused, n_splits == 1: argmax class per row
     float* prob;               // fused, n_splits == 1: max softmax probability per row
-    float4* partial;           // fused, n_splits > 1: [n_splits][m] (max, sum, idx bits, 0)
+    float4* partial;           // fused, n_splits > 1: [n_splits][m] (max, sum, idx bits, 0), log2 units
     float* logits;             // logits variant: [m][n]
     int* status;               // [2]
     unsigned long long timeout_ns;
     int debug_flags;
+    int poly_pairs;            // exp pairs per 64-class half computed on the FMA pipe (0,2,4,6,8)
 };
 
 struct PackParams {
@@ -54,6 +57,7 @@ struct PackParams {
     float* scales;             // [n]
     uint8_t* btiles;           // n_pad/128 tiles of 32 KB
     float2* colp;              // [n_pad]
+    float* ctab;               // [n_pad / 128][256]
 };
 
 // Kernel launchers (rechead_kernels.cu).

@@ -115,6 +115,11 @@ std::vector<int> injected_fault_slots() {
     return v;
 }
 
+int poly_pairs_setting() {
+    if (const char* s = std::getenv("RH_POLY_PAIRS")) return std::atoi(s);
+    return rh::kDefaultPolyPairs;
+}
+
 }  // namespace
 
 struct rh_ctx {
@@ -131,6 +136,7 @@ struct rh_weight {
         float* scales = nullptr;
         uint8_t* tiles = nullptr;
         float2* colp = nullptr;
+        float* ctab = nullptr;
     };
     std::vector<Per> per;
     std::vector<float> host_scales;  // QuantizedWeight::scales, kept to rebuild the bias table
@@ -160,6 +166,8 @@ int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per&
     p.merged_tail = w->g.merged;
     p.btiles = pw.tiles;
     p.colp = pw.colp;
+    p.ctab = pw.ctab;
+    p.poly_pairs = poly_pairs_setting();
     p.n_mblocks = n_mblocks;
     p.n_splits = n_splits;
     p.chunks_per_split = cps;
@@ -246,6 +254,13 @@ int upload_colp(rh_ctx* ctx, rh_weight* w, const float* bias) {
         else
             colp[j] = make_float2(0.0f, -INFINITY);
     }
+    const float kLog2e = 1.4426950408889634f;
+    std::vector<float> ctab((size_t)n_pad * 2);
+    for (int j = 0; j < n_pad; ++j) {
+        const int t = j / rh::kBlockN, r = j % rh::kBlockN;
+        ctab[(size_t)t * 256 + r] = j < w->n ? w->host_scales[j] * kLog2e : 0.0f;
+        ctab[(size_t)t * 256 + 128 + r] = j < w->n ? (bias ? bias[j] : 0.0f) * kLog2e : -INFINITY;
+    }
     for (auto& p : w->per) {
         Slot* slot = nullptr;
         for (auto& sp : ctx->slots)
@@ -254,6 +269,8 @@ int upload_colp(rh_ctx* ctx, rh_weight* w, const float* bias) {
         RH_CUDA(cudaSetDevice(p.device));
         // ordered after every kernel already queued on the slot stream that reads the table
         RH_CUDA(cudaMemcpyAsync(p.colp, colp.data(), colp.size() * sizeof(float2), cudaMemcpyHostToDevice,
+                                slot->stream));
+        RH_CUDA(cudaMemcpyAsync(p.ctab, ctab.data(), ctab.size() * sizeof(float), cudaMemcpyHostToDevice,
                                 slot->stream));
         RH_CUDA(cudaStreamSynchronize(slot->stream));
     }
@@ -396,6 +413,7 @@ int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const f
         RH_CUDA(cudaMalloc(&p.scales, (size_t)n * sizeof(float)));
         RH_CUDA(cudaMalloc(&p.tiles, (size_t)w->g.n_chunks * rh::kTileBytes));
         RH_CUDA(cudaMalloc(&p.colp, (size_t)n_pad * sizeof(float2)));
+        RH_CUDA(cudaMalloc(&p.ctab, (size_t)n_pad * 2 * sizeof(float)));
         w->per.push_back(p);
         float* d_w = nullptr;
         float* d_b = nullptr;
@@ -419,6 +437,7 @@ int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const f
         pp.scales = p.scales;
         pp.btiles = p.tiles;
         pp.colp = p.colp;
+        pp.ctab = p.ctab;
         RH_CUDA(rh::launch_pack(pp, s.stream));
         s.launches++;
         RH_CUDA(cudaStreamSynchronize(s.stream));
@@ -479,7 +498,7 @@ int rh_weight_dims(const rh_weight* w, int64_t* n, int64_t* k) {
 
 int64_t rh_weight_device_bytes(const rh_weight* w) {
     if (!w) return 0;
-    return w->n * w->k + w->n * 4 + (int64_t)w->g.n_chunks * (rh::kTileBytes + rh::kBlockN * 8);
+    return w->n * w->k + w->n * 4 + (int64_t)w->g.n_chunks * (rh::kTileBytes + rh::kBlockN * 16);
 }
 
 void rh_weight_free(rh_weight* w) {
@@ -491,6 +510,7 @@ void rh_weight_free(rh_weight* w) {
         cudaFree(p.scales);
         cudaFree(p.tiles);
         cudaFree(p.colp);
+        cudaFree(p.ctab);
     }
     delete w;
 }
@@ -716,6 +736,8 @@ int rh_head_decode_device_noalloc(rh_ctx* ctx, const rh_weight* w, int slot, con
     p.merged_tail = w->g.merged;
     p.btiles = pw->tiles;
     p.colp = pw->colp;
+    p.ctab = pw->ctab;
+    p.poly_pairs = poly_pairs_setting();
     p.n_mblocks = n_mblocks;
     p.n_splits = n_splits;
     p.chunks_per_split = cps;

@@ -4,7 +4,7 @@
 //  pack_kernel   QuantizedWeight::from_f32_transposed (src/ops/matmul.rs:1173-1202) on the
 //                GPU: per-class symmetric int8 + f32 scale, bit-exact; also writes the
 //                tensor-core image of the weight (fp16 tiles in shared-memory order) and the
-//                per-class (scale, bias) epilogue table.
+//                per-class epilogue tables.
 //  head_kernel   persistent, warp-specialised W8A32 projection. A (f32 features) is split
 //                into two fp16 parts in TMEM, weight tiles stream in through TMA bulk copies,
 //                tcgen05.mma accumulates in TMEM, and the epilogue applies scale + bias and
@@ -31,13 +31,17 @@ constexpr float kLog2e = 1.4426950408889634f;
 // ---------------------------------------------------------------- shared memory map
 // (offsets from the 1024-byte aligned base)
 constexpr uint32_t kOffB = 0;                                   // kStages weight tiles
-constexpr uint32_t kOffBars = kStages * kTileBytes;             // mbarriers (32 x 8 B)
-constexpr uint32_t kOffMisc = kOffBars + 32 * 8;                // [0] TMEM base, [1] abort flag
+constexpr uint32_t kOffBars = kStages * kTileBytes;             // mbarriers (48 x 8 B)
+constexpr uint32_t kOffMisc = kOffBars + 48 * 8;                // [0] TMEM base, [1] abort flag
 constexpr uint32_t kOffRho = kOffMisc + 32;                     // [4][128] f32 row de-scale
 constexpr uint32_t kOffQFlag = kOffRho + 4 * 128 * 4;           // [4][4] u32 "quadrant needs de-scale"
-constexpr uint32_t kOffMerge = kOffQFlag + 16 * 4;              // [2][128] float4
-constexpr uint32_t kSmemUsed = kOffMerge + 2 * 128 * 16;
+constexpr uint32_t kOffMerge = kOffQFlag + 16 * 4;              // [2][3][128] float4
+constexpr uint32_t kOffCtab = kOffMerge + 2 * 3 * 128 * 16;     // [4 slots][256] f32 class table
+constexpr uint32_t kCtabSlots = 4;
+constexpr uint32_t kCtabBytes = 256 * 4;
+constexpr uint32_t kSmemUsed = kOffCtab + kCtabSlots * kCtabBytes;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;               // + alignment slack
+static_assert(kOffCtab % 16 == 0, "bulk-copy destination alignment");
 
 // mbarrier indices
 constexpr int kBarBFull = 0;                     // [kStages] weight tile landed
@@ -45,18 +49,22 @@ constexpr int kBarBEmpty = kBarBFull + kStages;  // [kStages] MMAs reading the t
 constexpr int kBarAFull = kBarBEmpty + kStages;  // [2] A operand written to TMEM
 constexpr int kBarAEmpty = kBarAFull + 2;        // [2] MMAs of the unit done with A
 constexpr int kBarAccFull = kBarAEmpty + 2;      // [2] accumulator ready
-constexpr int kBarAccEmpty = kBarAccFull + 2;    // [2] accumulator drained by its epilogue group
+constexpr int kBarAccEmpty = kBarAccFull + 2;    // [2] accumulator drained by all four epilogue groups
 constexpr int kBarRhoFull = kBarAccEmpty + 2;    // [4] per-unit row de-scale written
-constexpr int kBarMFull = kBarRhoFull + 4;       // [2] group-1 partials staged for the merge
+constexpr int kBarMFull = kBarRhoFull + 4;       // [2] groups 1-3 partials staged for the merge
 constexpr int kBarMEmpty = kBarMFull + 2;        // [2] group 0 consumed them
 constexpr int kBarMmaDone = kBarMEmpty + 2;      // all MMAs retired (teardown)
-constexpr int kNumBars = kBarMmaDone + 1;
-static_assert(kNumBars <= 32, "barrier area");
+constexpr int kBarCtabFull = kBarMmaDone + 1;    // [4] class table of a tile landed
+constexpr int kBarCtabEmpty = kBarCtabFull + 4;  // [4] all epilogue groups are done with it
+constexpr int kNumBars = kBarCtabEmpty + 4;
+static_assert(kNumBars <= 48, "barrier area");
 
 // TMEM columns: A operand buffers [0,128) and [128,256), accumulators [256,384), [384,512).
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = 0;
 constexpr uint32_t kTmemAcc = 256;
+
+constexpr uint32_t kSleepHintNs = 20000;  // longest a waiting thread stays suspended per try
 
 struct Unit {
     int mb, sp, c0, c1;
@@ -74,12 +82,11 @@ __device__ __forceinline__ Unit unit_of(int u, const HeadParams& p) {
 // Bounded mbarrier wait. Gives up when another role has aborted or after timeout_ns, in
 // which case it raises the CTA abort flag and the device status; every role then leaves
 // its loop and the kernel tears down normally (TMEM freed, copies and MMAs drained).
-__device__ __noinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
-                                      const HeadParams& p, int where) {
-    if (mbar_try_wait(bar, parity)) return true;
+__device__ __noinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                           const HeadParams& p, int where) {
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, kSleepHintNs)) return true;
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > p.timeout_ns) {
             *abort_flag = 1u;
@@ -90,10 +97,16 @@ __device__ __noinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile ui
     }
 }
 
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                         const HeadParams& p, int where) {
+    if (mbar_try_wait(bar, parity)) return true;  // common case inline: no call on the hot path
+    return wait_bar_slow(bar, parity, abort_flag, p, where);
+}
+
 // Teardown wait: bounded by time only (used to drain work that is already in flight).
 __device__ __noinline__ void drain_bar(uint32_t bar, uint32_t parity, const HeadParams& p) {
     const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, kSleepHintNs)) {
         if (globaltimer_ns() - t0 > p.timeout_ns) {
             atomicOr(p.status, kDevTimeout);
             return;
@@ -129,51 +142,113 @@ __device__ __forceinline__ __half a_part(const float* arow, bool valid, int k, f
     return __float2half_rn(x - __half2float(h));
 }
 
-template <bool SCALED>
-__device__ __forceinline__ void fused_half(const uint32_t (&v)[64], const float2* __restrict__ cp, int col0,
-                                           float rho, float& run_max, float& run_sum, int& run_idx) {
-    float l[64];
-    float lmax = -CUDART_INF_F;
+// 2^x for x <= 0 on the FMA pipe, two lanes at once: x = j + f with j = rint(x) (magic-number
+// rounding) and f in [-1/2, 1/2]; 2^f from a degree-5 polynomial fitted for minimax relative
+// error on that interval (max 2.2e-7 in f32 Horner form, like ex2.approx); 2^j added to the
+// exponent field. x is clamped at -126 so the result stays a normal number (or ~1e-38).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    x.x = fmaxf(x.x, -126.0f);
+    x.y = fmaxf(x.y, -126.0f);
+    const float2 magic = make_float2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+    const float2 r = __fadd2_rn(x, magic);
+    const float2 j = __fadd2_rn(r, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);
+    float2 p = make_float2(1.3276457e-3f, 1.3276457e-3f);
+    p = __ffma2_rn(p, f, make_float2(9.6755419e-3f, 9.6755419e-3f));
+    p = __ffma2_rn(p, f, make_float2(5.5507135e-2f, 5.5507135e-2f));
+    p = __ffma2_rn(p, f, make_float2(2.4022120e-1f, 2.4022120e-1f));
+    p = __ffma2_rn(p, f, make_float2(6.9314694e-1f, 6.9314694e-1f));
+    p = __ffma2_rn(p, f, make_float2(1.0000001f, 1.0000001f));
+    // low bits of r hold j (two's complement); (r << 23) adds j to the exponent of p
+    const uint32_t bx = __float_as_uint(p.x) + (__float_as_uint(r.x) << 23);
+    const uint32_t by = __float_as_uint(p.y) + (__float_as_uint(r.y) << 23);
+    return make_float2(__uint_as_float(bx), __uint_as_float(by));
+}
+
+// 32 accumulator columns of one row: t = D*c + e (the logit in log2 units), then the online
+// (max, sum of 2^(t - max), first argmax) update. The exps are taken relative to the running
+// max from before these columns (so they need not wait for this quarter's max); the sum is
+// rescaled once if the max rose, and recomputed exactly in the rare case that it rose by more
+// than 64 (2^64 bounds every term, so nothing overflows). `cs`/`es` are the shared-memory class
+// table entries of these columns (shared-window addresses; warp-uniform, broadcast loads).
+template <bool SCALED, int NPOLY>
+__device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, uint32_t es, int col0,
+                                              float rho, float& run_max, float& run_sum, int& run_idx) {
+    float t[32];
 #pragma unroll
-    for (int i = 0; i < 64; i += 2) {
-        const float4 sb = __ldg(reinterpret_cast<const float4*>(cp + i));
-        float x0 = __uint_as_float(v[i]);
-        float x1 = __uint_as_float(v[i + 1]);
+    for (int i = 0; i < 32; i += 4) {
+        const float4 c4 = lds128(cs + 4u * i);
+        const float4 e4 = lds128(es + 4u * i);
+        float2 x01 = make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+        float2 x23 = make_float2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
         if (SCALED) {
-            x0 *= rho;
-            x1 *= rho;
+            x01 = __fmul2_rn(x01, make_float2(rho, rho));
+            x23 = __fmul2_rn(x23, make_float2(rho, rho));
         }
-        l[i] = fmaf(x0, sb.x, sb.y);
-        l[i + 1] = fmaf(x1, sb.z, sb.w);
-        lmax = fmaxf(lmax, fmaxf(l[i], l[i + 1]));
+        const float2 t01 = __ffma2_rn(x01, make_float2(c4.x, c4.y), make_float2(e4.x, e4.y));
+        const float2 t23 = __ffma2_rn(x23, make_float2(c4.z, c4.w), make_float2(e4.z, e4.w));
+        t[i] = t01.x;
+        t[i + 1] = t01.y;
+        t[i + 2] = t23.x;
+        t[i + 3] = t23.y;
     }
-    if (lmax > run_max) {
-        int first = 63;
+    float r1[11];
 #pragma unroll
-        for (int i = 63; i >= 0; --i)
-            if (l[i] == lmax) first = i;
-        run_sum *= ex2_approx((run_max - lmax) * kLog2e);
-        run_max = lmax;
+    for (int i = 0; i < 10; ++i) r1[i] = max3f(t[3 * i], t[3 * i + 1], t[3 * i + 2]);
+    r1[10] = fmaxf(t[30], t[31]);
+    const float qmax = max3f(max3f(r1[0], r1[1], r1[2]), max3f(r1[3], r1[4], r1[5]),
+                             max3f(max3f(r1[6], r1[7], r1[8]), r1[9], r1[10]));
+    if (run_max == -CUDART_INF_F) {  // first columns of this row in the unit: nothing to lag on
+        if (qmax == -CUDART_INF_F) return;
+        int first = 31;
+#pragma unroll
+        for (int i = 31; i >= 0; --i)
+            if (t[i] == qmax) first = i;
+        run_max = qmax;
         run_idx = col0 + first;
     }
-    if (run_max == -CUDART_INF_F) return;
-    const float c = -run_max * kLog2e;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    const float2 nm = make_float2(-run_max, -run_max);
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < 64; i += 4) {
-        s0 += ex2_approx(fmaf(l[i], kLog2e, c));
-        s1 += ex2_approx(fmaf(l[i + 1], kLog2e, c));
-        s2 += ex2_approx(fmaf(l[i + 2], kLog2e, c));
-        s3 += ex2_approx(fmaf(l[i + 3], kLog2e, c));
+    for (int i = 0; i < 32; i += 2) {
+        const float2 x = __fadd2_rn(make_float2(t[i], t[i + 1]), nm);
+        float2 e;
+        if ((i >> 1) < NPOLY)
+            e = exp2_poly2(x);
+        else
+            e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+        if ((i >> 1) & 1)
+            acc1 = __fadd2_rn(acc1, e);
+        else
+            acc0 = __fadd2_rn(acc0, e);
     }
-    run_sum += (s0 + s1) + (s2 + s3);
+    const float2 acc = __fadd2_rn(acc0, acc1);
+    float sq = acc.x + acc.y;
+    if (qmax > run_max) {
+        if (qmax - run_max > 64.0f) {  // exact recompute relative to the new max
+            sq = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sq += ex2_approx(t[i] - qmax);
+            run_sum = run_sum * ex2_approx(run_max - qmax) + sq;
+        } else {
+            run_sum = (run_sum + sq) * ex2_approx(run_max - qmax);
+        }
+        int first = 31;
+#pragma unroll
+        for (int i = 31; i >= 0; --i)
+            if (t[i] == qmax) first = i;
+        run_max = qmax;
+        run_idx = col0 + first;
+    } else {
+        run_sum += sq;
+    }
 }
 
 template <bool SCALED>
-__device__ __forceinline__ void logits_half(const uint32_t (&v)[64], const float2* __restrict__ cp, int col0,
-                                            float rho, float* __restrict__ out_row, int n) {
+__device__ __forceinline__ void logits_quarter(const uint32_t* v, const float2* __restrict__ cp, int col0,
+                                               float rho, float* __restrict__ out_row, int n) {
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
+    for (int i = 0; i < 32; ++i) {
         const float2 sb = __ldg(cp + i);
         float x = __uint_as_float(v[i]);
         if (SCALED) x *= rho;
@@ -181,13 +256,14 @@ __device__ __forceinline__ void logits_half(const uint32_t (&v)[64], const float
     }
 }
 
-// Merges two (max, sum of exp(l - max), first argmax) triples; ties keep the lower class.
+// Merges two (max, sum of 2^(t - max), first argmax) triples (log2 units); ties keep the
+// lower class index.
 __device__ __forceinline__ void combine(float& m0, float& s0, int& i0, float m1, float s1, int i1) {
     const bool take1 = (m1 > m0) || (m1 == m0 && i1 < i0);
     const float M = take1 ? m1 : m0;
     float S = 0.f;
-    if (m0 != -CUDART_INF_F) S += s0 * ex2_approx((m0 - M) * kLog2e);
-    if (m1 != -CUDART_INF_F) S += s1 * ex2_approx((m1 - M) * kLog2e);
+    if (m0 != -CUDART_INF_F) S += s0 * ex2_approx(m0 - M);
+    if (m1 != -CUDART_INF_F) S += s1 * ex2_approx(m1 - M);
     i0 = take1 ? i1 : i0;
     m0 = M;
     s0 = S;
@@ -228,12 +304,17 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackParams p) {
         const int kk = lane + 32 * i;
         if (real && kk < p.k) p.q[(size_t)j * p.k + kk] = (int8_t)qi;
     }
+    const int tile = j >> 7, r = j & 127;
     if (real && lane == 0) p.scales[j] = scale;
-    if (lane == 0) p.colp[j] = real ? make_float2(scale, p.bias ? p.bias[j] : 0.0f) : make_float2(0.0f, -CUDART_INF_F);
+    if (lane == 0) {
+        const float b = (real && p.bias) ? p.bias[j] : 0.0f;
+        p.colp[j] = real ? make_float2(scale, b) : make_float2(0.0f, -CUDART_INF_F);
+        p.ctab[(size_t)tile * 256 + r] = real ? scale * kLog2e : 0.0f;
+        p.ctab[(size_t)tile * 256 + 128 + r] = real ? b * kLog2e : -CUDART_INF_F;
+    }
 
     // tensor-core image: tile j/128, row r = j%128, K slot s -> byte offset
     // (s/64)*16384 + r*128 + (((s%64)/8) ^ (r%8))*16 + (s%8)*2
-    const int tile = j >> 7, r = j & 127;
     uint8_t* img = p.btiles + (size_t)tile * kTileBytes;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
@@ -258,11 +339,12 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackParams p) {
 // Warp roles (one CTA per SM, persistent over work units = (row block, class range)):
 //   warp 0      lane 0: weight-tile producer (TMA bulk copies into the smem ring)
 //   warp 1      TMEM allocator; lane 0: MMA issuer
-//   warps 2-3   idle
+//   warp 2      lane 0 (fused variant): class-table producer (TMA bulk copies, 4-slot ring)
+//   warp 3      idle
 //   warps 4-7   A converters: f32 rows -> (hi, lo) fp16 parts in TMEM, one lane quadrant each
-//   warps 8-11  epilogue group 0 (accumulator buffer 0), lane quadrants 0-3
-//   warps 12-15 epilogue group 1 (accumulator buffer 1)
-template <bool EMIT_LOGITS>
+//   warps 8-23  epilogue groups 0-3 (4 warps each, lane quadrants 0-3); group g drains
+//               columns [32g, 32g+32) of every accumulator tile
+template <bool EMIT_LOGITS, int NPOLY>
 __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_constant__ HeadParams p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -288,11 +370,15 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             mbar_init(bar(kBarAFull + i), 128);
             mbar_init(bar(kBarAEmpty + i), 1);
             mbar_init(bar(kBarAccFull + i), 1);
-            mbar_init(bar(kBarAccEmpty + i), 128);
-            mbar_init(bar(kBarMFull + i), 128);
+            mbar_init(bar(kBarAccEmpty + i), 512);
+            mbar_init(bar(kBarMFull + i), 384);
             mbar_init(bar(kBarMEmpty + i), 128);
         }
-        for (int i = 0; i < 4; ++i) mbar_init(bar(kBarRhoFull + i), 128);
+        for (int i = 0; i < 4; ++i) {
+            mbar_init(bar(kBarRhoFull + i), 128);
+            mbar_init(bar(kBarCtabFull + i), 1);
+            mbar_init(bar(kBarCtabEmpty + i), 512);
+        }
         mbar_init(bar(kBarMmaDone), 1);
         misc[1] = 0u;
         fence_mbar_init();
@@ -308,68 +394,101 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        if (lane == 0) {
+        // The whole warp runs the loop (uniform control flow); one elected lane issues.
+        uint32_t cc = 0, issued = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+            const Unit U = unit_of(u, p);
+            for (int c = U.c0; c < U.c1; ++c, ++cc) {
+                const int s = (int)(cc % kStages);
+                ok = __all_sync(0xffffffffu,
+                                wait_bar(bar(kBarBEmpty + s), ((cc / kStages) & 1u) ^ 1u, abort_flag, p, 1));
+                if (!ok) break;
+                if (p.debug_flags & kDebugStallProducer) continue;
+                if (elect_one()) {
+                    mbar_arrive_expect_tx(bar(kBarBFull + s), kTileBytes);
+                    bulk_copy_g2s(base + kOffB + (uint32_t)s * kTileBytes, p.btiles + (size_t)c * kTileBytes,
+                                  kTileBytes, bar(kBarBFull + s));
+                }
+                __syncwarp();
+                issued = cc + 1;
+            }
+        }
+        // Drain: the last copy issued into each stage must land before the CTA exits.
+        for (uint32_t s = 0; s < (uint32_t)kStages && s < issued; ++s) {
+            const uint32_t fills = (issued - 1 - s) / kStages + 1;
+            drain_bar(bar(kBarBFull + (int)s), (fills - 1) & 1u, p);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issuer
+        // Whole warp, uniform control flow; elect.sync inside the issue sequences.
+        const uint32_t idesc = idesc_f16_f32(128, 128);
+        const int steps = p.hi_steps + p.lo_steps;
+        // Per-step B descriptor offsets (16-byte units, added to the stage's descriptor).
+        uint32_t boff[16];
+#pragma unroll
+        for (int step = 0; step < 16; ++step) {
+            const int kc = step < p.hi_steps ? step : step - p.hi_steps;
+            boff[step] = ((uint32_t)(kc >> 2) * 16384u + (uint32_t)(kc & 3) * 32u) >> 4;
+        }
+        uint32_t cc = 0, uc = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
+            const Unit U = unit_of(u, p);
+            const uint32_t ab = uc & 1u;
+            ok = __all_sync(0xffffffffu, wait_bar(bar(kBarAFull + ab), (uc >> 1) & 1u, abort_flag, p, 2));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t a_tmem = tmem + kTmemA + ab * 128u;
+            for (int c = U.c0; c < U.c1; ++c, ++cc) {
+                const int s = (int)(cc % kStages);
+                const uint32_t buf = cc & 1u;
+                bool w = wait_bar(bar(kBarBFull + s), (cc / kStages) & 1u, abort_flag, p, 3);
+                w = w && wait_bar(bar(kBarAccEmpty + buf), ((cc >> 1) & 1u) ^ 1u, abort_flag, p, 4);
+                ok = __all_sync(0xffffffffu, w);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + kTmemAcc + buf * 128u;
+                const uint64_t bdesc0 = smem_desc_k_sw128(base + kOffB + (uint32_t)s * kTileBytes);
+#pragma unroll
+                for (int step = 0; step < 16; ++step) {
+                    if (step < steps)
+                        mma_f16_ts_warp(d_tmem, a_tmem + (uint32_t)step * 8u, bdesc0 + boff[step], idesc,
+                                        step > 0 ? 1u : 0u);
+                }
+                mma_commit_warp(bar(kBarBEmpty + s));
+                mma_commit_warp(bar(kBarAccFull + (int)buf));
+            }
+            if (!ok) break;
+            mma_commit_warp(bar(kBarAEmpty + (int)ab));
+        }
+        mma_commit_warp(bar(kBarMmaDone));
+        drain_bar(bar(kBarMmaDone), 0u, p);
+    } else if (warp == 2) {
+        // ---------------------------------------------------- class-table producer
+        if (!EMIT_LOGITS) {
             uint32_t cc = 0, issued = 0;
             bool ok = true;
             for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
                 const Unit U = unit_of(u, p);
                 for (int c = U.c0; c < U.c1; ++c, ++cc) {
-                    const int s = (int)(cc % kStages);
-                    if (!wait_bar(bar(kBarBEmpty + s), ((cc / kStages) & 1u) ^ 1u, abort_flag, p, 1)) {
-                        ok = false;
-                        break;
+                    const uint32_t slot = cc % kCtabSlots;
+                    ok = __all_sync(0xffffffffu, wait_bar(bar(kBarCtabEmpty + (int)slot),
+                                                          ((cc / kCtabSlots) & 1u) ^ 1u, abort_flag, p, 10));
+                    if (!ok) break;
+                    if (elect_one()) {
+                        mbar_arrive_expect_tx(bar(kBarCtabFull + (int)slot), kCtabBytes);
+                        bulk_copy_g2s(base + kOffCtab + slot * kCtabBytes, p.ctab + (size_t)c * 256, kCtabBytes,
+                                      bar(kBarCtabFull + (int)slot));
                     }
-                    if (p.debug_flags & kDebugStallProducer) continue;
-                    mbar_arrive_expect_tx(bar(kBarBFull + s), kTileBytes);
-                    bulk_copy_g2s(base + kOffB + (uint32_t)s * kTileBytes, p.btiles + (size_t)c * kTileBytes,
-                                  kTileBytes, bar(kBarBFull + s));
+                    __syncwarp();
                     issued = cc + 1;
                 }
             }
-            // Drain: the last copy issued into each stage must land before the CTA exits.
-            for (uint32_t s = 0; s < (uint32_t)kStages && s < issued; ++s) {
-                const uint32_t fills = (issued - 1 - s) / kStages + 1;
-                drain_bar(bar(kBarBFull + (int)s), (fills - 1) & 1u, p);
+            for (uint32_t s = 0; s < kCtabSlots && s < issued; ++s) {
+                const uint32_t fills = (issued - 1 - s) / kCtabSlots + 1;
+                drain_bar(bar(kBarCtabFull + (int)s), (fills - 1) & 1u, p);
             }
-        }
-    } else if (warp == 1) {
-        // ---------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16_f32(128, 128);
-            const int steps = p.hi_steps + p.lo_steps;
-            uint32_t cc = 0, uc = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
-                const Unit U = unit_of(u, p);
-                const uint32_t ab = uc & 1u;
-                if (!wait_bar(bar(kBarAFull + ab), (uc >> 1) & 1u, abort_flag, p, 2)) break;
-                tc_fence_after();
-                const uint32_t a_tmem = tmem + kTmemA + ab * 128u;
-                for (int c = U.c0; c < U.c1; ++c, ++cc) {
-                    const int s = (int)(cc % kStages);
-                    const uint32_t buf = cc & 1u;
-                    if (!wait_bar(bar(kBarBFull + s), (cc / kStages) & 1u, abort_flag, p, 3) ||
-                        !wait_bar(bar(kBarAccEmpty + buf), ((cc >> 1) & 1u) ^ 1u, abort_flag, p, 4)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t d_tmem = tmem + kTmemAcc + buf * 128u;
-                    const uint32_t b_smem = base + kOffB + (uint32_t)s * kTileBytes;
-                    for (int step = 0; step < steps; ++step) {
-                        const int kc = step < p.hi_steps ? step : step - p.hi_steps;
-                        const uint64_t bdesc =
-                            smem_desc_k_sw128(b_smem + (uint32_t)(kc >> 2) * 16384u + (uint32_t)(kc & 3) * 32u);
-                        mma_f16_ts(d_tmem, a_tmem + (uint32_t)step * 8u, bdesc, idesc, step > 0 ? 1u : 0u);
-                    }
-                    mma_commit(bar(kBarBEmpty + s));
-                    mma_commit(bar(kBarAccFull + (int)buf));
-                }
-                if (!ok) break;
-                mma_commit(bar(kBarAEmpty + (int)ab));
-            }
-            mma_commit(bar(kBarMmaDone));
-            drain_bar(bar(kBarMmaDone), 0u, p);
         }
     } else if (warp >= 4 && warp < 8) {
         // ----------------------------------------------------------- converters
@@ -426,6 +545,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         }
     } else if (warp >= 8) {
         // ------------------------------------------------------------- epilogue
+        // Group g owns columns [32g, 32g+32) of every accumulator tile: one 32-column TMEM load,
+        // the accumulator goes straight back to the MMA issuer, then the math runs from registers.
+        // Four groups give every SM sub-partition four independent warps of softmax work.
         const int g = (warp - 8) >> 2;
         const int q = warp & 3;
         const int r = q * 32 + lane;
@@ -438,68 +560,59 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             const long long row = (long long)U.mb * kBlockM + r;
             float run_max = -CUDART_INF_F, run_sum = 0.0f;
             int run_idx = 0;
-            bool have_rho = false, scaled = false;
-            float rho = 1.0f;
+            if (!wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6)) break;
+            const float rho = rho_s[slot * 128 + r];
+            const bool scaled = qflag_s[slot * 4 + q] != 0u;
             for (int c = U.c0; c < U.c1; ++c, ++cc) {
                 const uint32_t buf = cc & 1u;
-                if ((int)buf != g) continue;
-                if (!have_rho) {
-                    if (!wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6)) {
-                        ok = false;
-                        break;
-                    }
-                    rho = rho_s[slot * 128 + r];
-                    scaled = qflag_s[slot * 4 + q] != 0u;
-                    have_rho = true;
+                const uint32_t cslot = cc % kCtabSlots;
+                if (!EMIT_LOGITS &&
+                    !wait_bar(bar(kBarCtabFull + (int)cslot), (cc / kCtabSlots) & 1u, abort_flag, p, 11)) {
+                    ok = false;
+                    break;
                 }
                 if (!wait_bar(bar(kBarAccFull + (int)buf), (cc >> 1) & 1u, abort_flag, p, 7)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t taddr = tmem + lane_base + kTmemAcc + buf * 128u;
-                const float2* cp = p.colp + (size_t)c * kBlockN;
-                const int col0 = c * kBlockN;
-                uint32_t v[64];
-                tmem_ld32x32b_x64_wait(taddr, v);
-                if (EMIT_LOGITS) {
-                    float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
-                    if (row < p.m) {
-                        if (scaled) logits_half<true>(v, cp, col0, rho, out_row, p.n);
-                        else logits_half<false>(v, cp, col0, rho, out_row, p.n);
-                    }
-                } else {
-                    if (scaled) fused_half<true>(v, cp, col0, rho, run_max, run_sum, run_idx);
-                    else fused_half<false>(v, cp, col0, rho, run_max, run_sum, run_idx);
-                }
-                tmem_ld32x32b_x64_wait(taddr + 64u, v);
+                uint32_t v[32];
+                tmem_ld32x32b_x32_wait(tmem + lane_base + kTmemAcc + buf * 128u + (uint32_t)(32 * g), v);
                 tc_fence_before();
                 mbar_arrive(bar(kBarAccEmpty + (int)buf));
+                const int col0 = c * kBlockN + 32 * g;
                 if (EMIT_LOGITS) {
+                    const float2* cp = p.colp + (size_t)col0;
                     float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
                     if (row < p.m) {
-                        if (scaled) logits_half<true>(v, cp + 64, col0 + 64, rho, out_row, p.n);
-                        else logits_half<false>(v, cp + 64, col0 + 64, rho, out_row, p.n);
+                        if (scaled) logits_quarter<true>(v, cp, col0, rho, out_row, p.n);
+                        else logits_quarter<false>(v, cp, col0, rho, out_row, p.n);
                     }
                 } else {
-                    if (scaled) fused_half<true>(v, cp + 64, col0 + 64, rho, run_max, run_sum, run_idx);
-                    else fused_half<false>(v, cp + 64, col0 + 64, rho, run_max, run_sum, run_idx);
+                    const uint32_t cs = base + kOffCtab + cslot * kCtabBytes + 4u * (uint32_t)(32 * g);
+                    if (scaled)
+                        fused_quarter<true, NPOLY / 2>(v, cs, cs + 512u, col0, rho, run_max, run_sum, run_idx);
+                    else
+                        fused_quarter<false, NPOLY / 2>(v, cs, cs + 512u, col0, rho, run_max, run_sum, run_idx);
+                    mbar_arrive(bar(kBarCtabEmpty + (int)cslot));
                 }
             }
             if (!ok) break;
             if (!EMIT_LOGITS) {
-                // Merge the two groups' partial rows for this unit through shared memory.
+                // Merge the four groups' partial rows for this unit through shared memory.
                 const uint32_t mb2 = uc & 1u;
-                float4* mg = merge_s + mb2 * 128;
-                if (g == 1) {
+                float4* mg = merge_s + mb2 * 384;
+                if (g != 0) {
                     if (!wait_bar(bar(kBarMEmpty + (int)mb2), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 8)) break;
-                    mg[r] = make_float4(run_max, run_sum, __int_as_float(run_idx), 0.0f);
+                    mg[(g - 1) * 128 + r] = make_float4(run_max, run_sum, __int_as_float(run_idx), 0.0f);
                     mbar_arrive(bar(kBarMFull + (int)mb2));
                 } else {
                     if (!wait_bar(bar(kBarMFull + (int)mb2), (uc >> 1) & 1u, abort_flag, p, 9)) break;
-                    const float4 o = mg[r];
+                    const float4 o1 = mg[r], o2 = mg[128 + r], o3 = mg[256 + r];
                     mbar_arrive(bar(kBarMEmpty + (int)mb2));
-                    combine(run_max, run_sum, run_idx, o.x, o.y, __float_as_int(o.z));
+                    combine(run_max, run_sum, run_idx, o1.x, o1.y, __float_as_int(o1.z));
+                    combine(run_max, run_sum, run_idx, o2.x, o2.y, __float_as_int(o2.z));
+                    combine(run_max, run_sum, run_idx, o3.x, o3.y, __float_as_int(o3.z));
                     if (row < p.m) {
                         if (p.n_splits == 1) {
                             p.idx[row] = run_idx;
@@ -540,11 +653,19 @@ __global__ void __launch_bounds__(256) merge_kernel(const float4* __restrict__ p
 // ------------------------------------------------------------------ launchers
 size_t head_smem_bytes() { return kSmemBytes; }
 
+template <bool L, int NP>
+static cudaError_t set_smem_attr() {
+    return cudaFuncSetAttribute(head_kernel<L, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+}
+
 cudaError_t head_kernel_setup() {
-    cudaError_t e = cudaFuncSetAttribute(head_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBytes);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(head_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    cudaError_t e;
+    if ((e = set_smem_attr<true, 0>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<false, 0>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<false, 2>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<false, 4>()) != cudaSuccess) return e;
+    if ((e = set_smem_attr<false, 6>()) != cudaSuccess) return e;
+    return set_smem_attr<false, 8>();
 }
 
 cudaError_t launch_pack(const PackParams& p, cudaStream_t stream) {
@@ -556,10 +677,17 @@ cudaError_t launch_pack(const PackParams& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_head(const HeadParams& p, bool emit_logits, int grid, cudaStream_t stream) {
-    if (emit_logits)
-        head_kernel<true><<<grid, kHeadThreads, kSmemBytes, stream>>>(p);
-    else
-        head_kernel<false><<<grid, kHeadThreads, kSmemBytes, stream>>>(p);
+    if (emit_logits) {
+        head_kernel<true, 0><<<grid, kHeadThreads, kSmemBytes, stream>>>(p);
+    } else {
+        switch (p.poly_pairs) {
+            case 0: head_kernel<false, 0><<<grid, kHeadThreads, kSmemBytes, stream>>>(p); break;
+            case 2: head_kernel<false, 2><<<grid, kHeadThreads, kSmemBytes, stream>>>(p); break;
+            case 6: head_kernel<false, 6><<<grid, kHeadThreads, kSmemBytes, stream>>>(p); break;
+            case 8: head_kernel<false, 8><<<grid, kHeadThreads, kSmemBytes, stream>>>(p); break;
+            default: head_kernel<false, 4><<<grid, kHeadThreads, kSmemBytes, stream>>>(p); break;
+        }
+    }
     return cudaGetLastError();
 }
 

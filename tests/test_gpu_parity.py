@@ -253,6 +253,16 @@ def test_fused_cfg4_precision_stress(rh, ctx, oracle):
     assert np.all(ref["gap"][wl.tie_rows] < 1.2e-4)  # the construction did build near-ties
 
 
+@pytest.mark.parametrize("pairs", ["0", "2", "4", "6", "8"])
+def test_fused_every_exp_offload_setting(rh, ctx, oracle, monkeypatch, pairs):
+    """Each instantiation of the epilogue (0-8 exp pairs of every 64 on the FMA-pipe
+    polynomial, the rest on MUFU ex2) meets the same parity bar."""
+    from rust_ppocrv6_b200 import workloads
+
+    monkeypatch.setenv("RH_POLY_PAIRS", pairs)
+    fused_case(rh, ctx, oracle, workloads.make(1, scale=0.25), f"poly={pairs}")
+
+
 def test_fused_matches_logits_path(rh, ctx, oracle):
     """The two epilogues share the mainloop: argmax of the GPU logits == fused idx."""
     from rust_ppocrv6_b200 import workloads
