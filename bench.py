@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2")
-    ap.add_argument("--cpu-sample-lines", type=int, default=48)
+    ap.add_argument("--cpu-sample-lines", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 

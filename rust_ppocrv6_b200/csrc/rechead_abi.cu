@@ -55,6 +55,8 @@ struct Slot {
     int device = 0;
     int sms = 0;
     cudaStream_t stream = nullptr;
+    cudaStream_t copy_stream = nullptr;  // host-to-device copies that overlap the kernels
+    cudaEvent_t copied = nullptr;
     int* d_status = nullptr;
     DevBuf a, idx, prob, out, partial;
     std::mutex mu;
@@ -223,9 +225,9 @@ int run_host_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, 
     if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
     const size_t a_bytes = (size_t)rows * (size_t)w->k * sizeof(float);
     RH_CUDA(s.a.ensure(a_bytes));
-    RH_CUDA(cudaMemcpyAsync(s.a.p, a, a_bytes, cudaMemcpyHostToDevice, s.stream));
     const bool emit_logits = logits != nullptr;
     if (emit_logits) {
+        RH_CUDA(cudaMemcpyAsync(s.a.p, a, a_bytes, cudaMemcpyHostToDevice, s.stream));
         const size_t o_bytes = (size_t)rows * (size_t)w->n * sizeof(float);
         RH_CUDA(s.out.ensure(o_bytes));
         int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, nullptr, nullptr, (float*)s.out.p, true,
@@ -233,13 +235,27 @@ int run_host_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, 
         if (rc) return rc;
         RH_CUDA(cudaMemcpyAsync(logits, s.out.p, o_bytes, cudaMemcpyDeviceToHost, s.stream));
     } else {
+        // Pipelined: pieces of one full wave of 128-row blocks. The copy of piece i+1 runs on the
+        // copy stream while piece i computes; an event hands each piece to the compute stream.
         RH_CUDA(s.idx.ensure((size_t)rows * sizeof(int32_t)));
         RH_CUDA(s.prob.ensure((size_t)rows * sizeof(float)));
-        int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, (int32_t*)s.idx.p, (float*)s.prob.p,
-                              nullptr, false, s.stream);
-        if (rc) return rc;
-        RH_CUDA(cudaMemcpyAsync(idx, s.idx.p, (size_t)rows * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
-        RH_CUDA(cudaMemcpyAsync(prob, s.prob.p, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+        const int64_t piece = (int64_t)s.sms * rh::kBlockM;
+        const size_t row_bytes = (size_t)w->k * sizeof(float);
+        for (int64_t r0 = 0; r0 < rows; r0 += piece) {
+            const int64_t n = std::min(piece, rows - r0);
+            const float* src = a + (size_t)r0 * (size_t)w->k;
+            float* dst = (float*)s.a.p + (size_t)r0 * (size_t)w->k;
+            RH_CUDA(cudaMemcpyAsync(dst, src, (size_t)n * row_bytes, cudaMemcpyHostToDevice, s.copy_stream));
+            RH_CUDA(cudaEventRecord(s.copied, s.copy_stream));
+            RH_CUDA(cudaStreamWaitEvent(s.stream, s.copied, 0));
+            int rc = enqueue_head(ctx, w, s, *pw, dst, n, (int32_t*)s.idx.p + r0, (float*)s.prob.p + r0, nullptr,
+                                  false, s.stream);
+            if (rc) return rc;
+            RH_CUDA(cudaMemcpyAsync(idx + r0, (int32_t*)s.idx.p + r0, (size_t)n * sizeof(int32_t),
+                                    cudaMemcpyDeviceToHost, s.stream));
+            RH_CUDA(cudaMemcpyAsync(prob + r0, (float*)s.prob.p + r0, (size_t)n * sizeof(float),
+                                    cudaMemcpyDeviceToHost, s.stream));
+        }
     }
     RH_CUDA(cudaStreamSynchronize(s.stream));
     return read_status(s);
@@ -352,6 +368,8 @@ int rh_ctx_create(const int* devices, int n_devices, rh_ctx** out) {
         RH_CUDA(cudaSetDevice(d));
         RH_CUDA(rh::head_kernel_setup());
         RH_CUDA(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+        RH_CUDA(cudaStreamCreateWithFlags(&s->copy_stream, cudaStreamNonBlocking));
+        RH_CUDA(cudaEventCreateWithFlags(&s->copied, cudaEventDisableTiming));
         RH_CUDA(cudaMalloc(&s->d_status, 2 * sizeof(int)));
         RH_CUDA(cudaMemsetAsync(s->d_status, 0, 2 * sizeof(int), s->stream));
         RH_CUDA(cudaStreamSynchronize(s->stream));
@@ -372,6 +390,9 @@ void rh_ctx_destroy(rh_ctx* ctx) {
         s->out.release();
         s->partial.release();
         if (s->d_status) cudaFree(s->d_status);
+        if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
+        if (s->copied) cudaEventDestroy(s->copied);
+        if (s->copy_stream) cudaStreamDestroy(s->copy_stream);
         if (s->stream) cudaStreamDestroy(s->stream);
     }
     delete ctx;
