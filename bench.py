@@ -155,16 +155,21 @@ def measured_peak_tflops():
 
 
 def profiled_traffic():
+    """DRAM bytes (read + write) of one cfg2 head-kernel launch, from the committed ncu summary."""
+    import re
+
     try:
-        with open(os.path.join(ROOT, "profiles", "head_kernel_traffic.json")) as f:
-            return json.load(f)
-    except Exception:
+        with open(os.path.join(ROOT, "profiles", "head_kernel_cfg2_ncu_full.md")) as f:
+            m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", f.read(), re.M)
+        return int(m.group(1)) if m else None
+    except OSError:
         return None
 
 
-def cpu_reference(lines_off: np.ndarray, x: np.ndarray, w_t, bias, sample_lines: int, reps: int = 1):
+def cpu_reference(lines_off: np.ndarray, x: np.ndarray, w_t, bias, sample_lines: int, target_s: float = 10.0):
     """Times the oracle port (the reference's AVX2 path, restated) on `sample_lines` lines
-    of the workload with every host thread. Returns (timesteps/s, threads, rows, seconds)."""
+    of the workload with every host thread, repeating the sample until about `target_s`
+    seconds of CPU work have run. Returns (timesteps/s, threads, rows per pass, passes, seconds)."""
     from oracle import oracle
 
     q, s = oracle.pack(w_t)
@@ -173,12 +178,14 @@ def cpu_reference(lines_off: np.ndarray, x: np.ndarray, w_t, bias, sample_lines:
     rows = int(off[-1])
     xs = np.ascontiguousarray(x[:rows])
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
-    oracle.head_decode(xs[: int(off[1])], off[:2], q, s, bias, threads=threads)  # warm caches
+    t0 = time.perf_counter()
+    oracle.head_decode(xs, off, q, s, bias, threads=threads)  # warm caches, size the repeat count
+    reps = max(1, int(np.ceil(target_s / max(time.perf_counter() - t0, 1e-3))))
     t0 = time.perf_counter()
     for _ in range(reps):
         oracle.head_decode(xs, off, q, s, bias, threads=threads)
     dt = time.perf_counter() - t0
-    return rows * reps / dt, threads, rows, dt
+    return rows * reps / dt, threads, rows, reps, dt
 
 
 def run_reference_arm(args, world, rank):
@@ -316,7 +323,9 @@ def main():
     traffic = profiled_traffic()
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "peak_source": peak_src,
-                "traffic": None if traffic is None else traffic["bytes_per_launch_cfg2"],
+                "traffic": traffic if args.workload == "cfg2" else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one cfg2 launch "
+                                  "(profiles/head_kernel_cfg2_ncu_full.md)",
                 "tf32_equiv_frac": achieved / (peak / 2),
                 "note": "achieved = 2*K*N*rows per step / device time per step (head + merge kernels)"}
 
@@ -334,10 +343,10 @@ def main():
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, threads, srows, dt = cpu_reference(off, x_host, w_t, bias, args.cpu_sample_lines)
+        v, threads, srows, reps, dt = cpu_reference(off, x_host, w_t, bias, args.cpu_sample_lines)
         out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                               "sample": f"{srows} timesteps ({args.cpu_sample_lines} lines of the workload), "
-                                         f"{dt:.2f} s wall"}
+                               "sample": f"{srows} timesteps ({args.cpu_sample_lines} lines of the workload) "
+                                         f"x {reps} passes, {dt:.1f} s wall"}
     qw.free()
     ctx.close()
     if rank == 0:

@@ -18,7 +18,10 @@ constexpr int kDevTimeout = 1;
 // Test-only: the weight producer never fills its stages, so every consumer's bounded wait
 // runs out and the kernel must return kDevTimeout with the context intact.
 constexpr int kDebugStallProducer = 1;
-constexpr int kDefaultPolyPairs = 4;
+// Pairs of columns per 32-column quarter whose 2^x runs on the FMA pipe instead of MUFU.
+// The epilogue is instruction-issue bound rather than MUFU bound, so the polynomial's extra
+// instructions cost more than the MUFU time they save: 0 measured fastest on cfg2.
+constexpr int kDefaultPolyPairs = 0;
 
 struct HeadParams {
     const float* a;            // [m][k] timestep features (rows packed densely)
