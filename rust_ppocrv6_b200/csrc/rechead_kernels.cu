@@ -39,7 +39,8 @@ constexpr uint32_t kOffMerge = kOffQFlag + 16 * 4;              // [2][3][128] f
 constexpr uint32_t kOffCtab = kOffMerge + 2 * 3 * 128 * 16;     // [4 slots][256] f32 class table
 constexpr uint32_t kCtabSlots = 4;
 constexpr uint32_t kCtabBytes = 256 * 4;
-constexpr uint32_t kSmemUsed = kOffCtab + kCtabSlots * kCtabBytes;
+constexpr uint32_t kOffRowMax = kOffCtab + kCtabSlots * kCtabBytes;  // [128] u64 (unit tag, ordered max)
+constexpr uint32_t kSmemUsed = kOffRowMax + 128 * 8;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;               // + alignment slack
 static_assert(kOffCtab % 16 == 0, "bulk-copy destination alignment");
 
@@ -165,15 +166,38 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     return make_float2(__uint_as_float(bx), __uint_as_float(by));
 }
 
+// Order-preserving map of a (non-NaN) f32 onto u32: a < b  <=>  ord(a) < ord(b).
+__device__ __forceinline__ uint32_t f32_ord(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Per-row state of one epilogue group over a work unit.
+//   off, sum : sum = sum of 2^(t - off) over every column seen; off = their max.
+//   best, idx: max and first argmax over the columns whose quarter reached the row's shared
+//              threshold (see fused_quarter); the group that holds the unit's maximum always
+//              tracks it, so the unit's (max, argmax) is the best of the groups' (best, idx).
+struct RowState {
+    float off, sum, best;
+    int idx;
+};
+
 // 32 accumulator columns of one row: t = D*c + e (the logit in log2 units), then the online
-// (max, sum of 2^(t - max), first argmax) update. The exps are taken relative to the running
-// max from before these columns (so they need not wait for this quarter's max); the sum is
-// rescaled once if the max rose, and recomputed exactly in the rare case that it rose by more
-// than 64 (2^64 bounds every term, so nothing overflows). `cs`/`es` are the shared-memory class
-// table entries of these columns (shared-window addresses; warp-uniform, broadcast loads).
-template <bool SCALED, int NPOLY>
+// update of `st`. The exps are taken relative to the running max from before these columns
+// (so they need not wait for this quarter's max); the sum is rescaled once if the max rose,
+// and recomputed exactly in the rare case that it rose by more than 64 (2^64 bounds every
+// term, so nothing overflows). `cs`/`es` are the shared-memory class table entries of these
+// columns (shared-window addresses; warp-uniform, broadcast loads).
+//
+// First-argmax search: a quarter is searched only when its max beats the group's own best
+// AND reaches the row's threshold `rowmax` - the largest best any of the four groups has
+// published for this row in this unit (a 64-bit word: unit tag above, f32_ord(best) below;
+// a word with another tag counts as no threshold). The threshold never exceeds the unit's
+// true maximum, so the quarter that holds the first maximum is always searched, while the
+// other groups stop searching quarters that cannot win.
+template <bool SCALED, int NPOLY, bool FIRST>
 __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, uint32_t es, int col0,
-                                              float rho, float& run_max, float& run_sum, int& run_idx) {
+                                              float rho, uint32_t rowmax, uint32_t tag, RowState& st) {
     float t[32];
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
@@ -198,16 +222,13 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
     r1[10] = fmaxf(t[30], t[31]);
     const float qmax = max3f(max3f(r1[0], r1[1], r1[2]), max3f(r1[3], r1[4], r1[5]),
                              max3f(max3f(r1[6], r1[7], r1[8]), r1[9], r1[10]));
-    if (run_max == -CUDART_INF_F) {  // first columns of this row in the unit: nothing to lag on
-        if (qmax == -CUDART_INF_F) return;
-        int first = 31;
-#pragma unroll
-        for (int i = 31; i >= 0; --i)
-            if (t[i] == qmax) first = i;
-        run_max = qmax;
-        run_idx = col0 + first;
+    if constexpr (FIRST) {  // first columns of this row in the unit: offset = their max
+        if (qmax == -CUDART_INF_F) return;  // padded classes only
+        st.off = qmax;
     }
-    const float2 nm = make_float2(-run_max, -run_max);
+    // The offset is known before this quarter (FIRST: qmax), so the exps need not wait for
+    // the max tree of the other branch and both run interleaved.
+    const float2 nm = make_float2(-st.off, -st.off);
     float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
@@ -224,23 +245,34 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
     }
     const float2 acc = __fadd2_rn(acc0, acc1);
     float sq = acc.x + acc.y;
-    if (qmax > run_max) {
-        if (qmax - run_max > 64.0f) {  // exact recompute relative to the new max
+    if constexpr (FIRST) {
+        st.sum = sq;
+    } else if (qmax > st.off) {
+        if (qmax - st.off > 64.0f) {  // exact recompute relative to the new max
             sq = 0.0f;
 #pragma unroll
             for (int i = 0; i < 32; ++i) sq += ex2_approx(t[i] - qmax);
-            run_sum = run_sum * ex2_approx(run_max - qmax) + sq;
+            st.sum = (st.off == -CUDART_INF_F ? 0.0f : st.sum * ex2_approx(st.off - qmax)) + sq;
         } else {
-            run_sum = (run_sum + sq) * ex2_approx(run_max - qmax);
+            st.sum = (st.sum + sq) * ex2_approx(st.off - qmax);
         }
-        int first = 31;
-#pragma unroll
-        for (int i = 31; i >= 0; --i)
-            if (t[i] == qmax) first = i;
-        run_max = qmax;
-        run_idx = col0 + first;
+        st.off = qmax;
     } else {
-        run_sum += sq;
+        st.sum += sq;
+    }
+    if (qmax > st.best) {
+        const unsigned long long w = lds_u64(rowmax);
+        const uint32_t thr = (uint32_t)(w >> 32) == tag ? (uint32_t)w : 0u;
+        const uint32_t qo = f32_ord(qmax);
+        if (qo >= thr) {
+            int first = 31;
+#pragma unroll
+            for (int i = 31; i >= 0; --i)
+                if (t[i] == qmax) first = i;
+            st.best = qmax;
+            st.idx = col0 + first;
+            if (qo > thr) atom_max_shared_u64(rowmax, ((unsigned long long)tag << 32) | qo);
+        }
     }
 }
 
@@ -382,6 +414,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         mbar_init(bar(kBarMmaDone), 1);
         misc[1] = 0u;
         fence_mbar_init();
+    }
+    if (threadIdx.x < 128) {  // row thresholds start with tag 0: no unit has published yet
+        reinterpret_cast<unsigned long long*>(gbase + kOffRowMax)[threadIdx.x] = 0ull;
     }
     if (warp == 1) {
         tmem_alloc(base + kOffMisc, kTmemCols);
@@ -558,8 +593,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             const Unit U = unit_of(u, p);
             const uint32_t slot = uc & 3u;
             const long long row = (long long)U.mb * kBlockM + r;
-            float run_max = -CUDART_INF_F, run_sum = 0.0f;
-            int run_idx = 0;
+            RowState st{-CUDART_INF_F, 0.0f, -CUDART_INF_F, 0};
+            const uint32_t tag = uc + 1u;  // row thresholds of earlier units carry smaller tags
+            const uint32_t rowmax = base + kOffRowMax + 8u * (uint32_t)r;
             if (!wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6)) break;
             const float rho = rho_s[slot * 128 + r];
             const bool scaled = qflag_s[slot * 4 + q] != 0u;
@@ -590,10 +626,17 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                     }
                 } else {
                     const uint32_t cs = base + kOffCtab + cslot * kCtabBytes + 4u * (uint32_t)(32 * g);
-                    if (scaled)
-                        fused_quarter<true, NPOLY / 2>(v, cs, cs + 512u, col0, rho, run_max, run_sum, run_idx);
-                    else
-                        fused_quarter<false, NPOLY / 2>(v, cs, cs + 512u, col0, rho, run_max, run_sum, run_idx);
+                    if (c == U.c0) {
+                        if (scaled)
+                            fused_quarter<true, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                        else
+                            fused_quarter<false, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                    } else {
+                        if (scaled)
+                            fused_quarter<true, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                        else
+                            fused_quarter<false, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                    }
                     mbar_arrive(bar(kBarCtabEmpty + (int)cslot));
                 }
             }
@@ -604,22 +647,33 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 float4* mg = merge_s + mb2 * 384;
                 if (g != 0) {
                     if (!wait_bar(bar(kBarMEmpty + (int)mb2), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 8)) break;
-                    mg[(g - 1) * 128 + r] = make_float4(run_max, run_sum, __int_as_float(run_idx), 0.0f);
+                    mg[(g - 1) * 128 + r] = make_float4(st.off, st.sum, st.best, __int_as_float(st.idx));
                     mbar_arrive(bar(kBarMFull + (int)mb2));
                 } else {
                     if (!wait_bar(bar(kBarMFull + (int)mb2), (uc >> 1) & 1u, abort_flag, p, 9)) break;
                     const float4 o1 = mg[r], o2 = mg[128 + r], o3 = mg[256 + r];
                     mbar_arrive(bar(kBarMEmpty + (int)mb2));
-                    combine(run_max, run_sum, run_idx, o1.x, o1.y, __float_as_int(o1.z));
-                    combine(run_max, run_sum, run_idx, o2.x, o2.y, __float_as_int(o2.z));
-                    combine(run_max, run_sum, run_idx, o3.x, o3.y, __float_as_int(o3.z));
+                    // Unit maximum = the largest offset; the argmax comes from the group(s)
+                    // whose tracked best equals it (ties: lower class index).
+                    const float M = fmaxf(fmaxf(st.off, o1.x), fmaxf(o2.x, o3.x));
+                    float S = 0.0f;
+                    if (st.off != -CUDART_INF_F) S += st.sum * ex2_approx(st.off - M);
+                    if (o1.x != -CUDART_INF_F) S += o1.y * ex2_approx(o1.x - M);
+                    if (o2.x != -CUDART_INF_F) S += o2.y * ex2_approx(o2.x - M);
+                    if (o3.x != -CUDART_INF_F) S += o3.y * ex2_approx(o3.x - M);
+                    int I = 0x7fffffff;
+                    if (st.best == M) I = st.idx;
+                    if (o1.z == M) I = min(I, __float_as_int(o1.w));
+                    if (o2.z == M) I = min(I, __float_as_int(o2.w));
+                    if (o3.z == M) I = min(I, __float_as_int(o3.w));
+                    if (I == 0x7fffffff) I = 0;  // no class at all (cannot happen for a real unit)
                     if (row < p.m) {
                         if (p.n_splits == 1) {
-                            p.idx[row] = run_idx;
-                            p.prob[row] = 1.0f / run_sum;
+                            p.idx[row] = I;
+                            p.prob[row] = 1.0f / S;
                         } else {
                             p.partial[(size_t)U.sp * (size_t)p.m + (size_t)row] =
-                                make_float4(run_max, run_sum, __int_as_float(run_idx), 0.0f);
+                                make_float4(M, S, __int_as_float(I), 0.0f);
                         }
                     }
                 }

@@ -200,6 +200,16 @@ __device__ __forceinline__ float4 lds128(uint32_t addr) {
     return v;
 }
 
+// 64-bit shared-memory load / atomic maximum through the shared window.
+__device__ __forceinline__ unsigned long long lds_u64(uint32_t addr) {
+    unsigned long long v;
+    asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void atom_max_shared_u64(uint32_t addr, unsigned long long v) {
+    asm volatile("red.shared.max.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+
 // Three-input maximum (sm_100): NaN operands are ignored like fmaxf.
 __device__ __forceinline__ float max3f(float a, float b, float c) {
     float d;
