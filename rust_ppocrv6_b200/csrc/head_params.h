@@ -11,7 +11,8 @@ constexpr int kBlockN = 128;                  // classes per weight tile / accum
 constexpr int kPadK = 128;                    // K extent of a weight tile (K <= 128 supported)
 constexpr int kTileBytes = kBlockN * kPadK * 2;  // one fp16 weight tile: 32 KB
 constexpr int kStages = 4;                    // weight-tile ring depth in shared memory
-constexpr int kHeadThreads = 768;             // 24 warps, see head_kernel
+constexpr int kEpiGroups = 6;                 // epilogue warp groups (4 warps each)
+constexpr int kHeadThreads = 32 * (8 + 4 * kEpiGroups);  // 32 warps, see head_kernel
 
 // Device status word bits (status[0]); status[1] records which wait gave up.
 constexpr int kDevTimeout = 1;

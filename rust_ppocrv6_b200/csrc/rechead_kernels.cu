@@ -35,8 +35,8 @@ constexpr uint32_t kOffBars = kStages * kTileBytes;             // mbarriers (48
 constexpr uint32_t kOffMisc = kOffBars + 48 * 8;                // [0] TMEM base, [1] abort flag
 constexpr uint32_t kOffRho = kOffMisc + 32;                     // [4][128] f32 row de-scale
 constexpr uint32_t kOffQFlag = kOffRho + 4 * 128 * 4;           // [4][4] u32 "quadrant needs de-scale"
-constexpr uint32_t kOffMerge = kOffQFlag + 16 * 4;              // [2][3][128] float4
-constexpr uint32_t kOffCtab = kOffMerge + 2 * 3 * 128 * 16;     // [4 slots][256] f32 class table
+constexpr uint32_t kOffMerge = kOffQFlag + 16 * 4;              // [2][kEpiGroups-1][128] float4
+constexpr uint32_t kOffCtab = kOffMerge + 2 * (kEpiGroups - 1) * 128 * 16;  // [4 slots][256] f32 class table
 constexpr uint32_t kCtabSlots = 4;
 constexpr uint32_t kCtabBytes = 256 * 4;
 constexpr uint32_t kOffRowMax = kOffCtab + kCtabSlots * kCtabBytes;  // [128] u64 (unit tag, ordered max)
@@ -50,9 +50,9 @@ constexpr int kBarBEmpty = kBarBFull + kStages;  // [kStages] MMAs reading the t
 constexpr int kBarAFull = kBarBEmpty + kStages;  // [2] A operand written to TMEM
 constexpr int kBarAEmpty = kBarAFull + 2;        // [2] MMAs of the unit done with A
 constexpr int kBarAccFull = kBarAEmpty + 2;      // [2] accumulator ready
-constexpr int kBarAccEmpty = kBarAccFull + 2;    // [2] accumulator drained by all four epilogue groups
+constexpr int kBarAccEmpty = kBarAccFull + 2;    // [2] accumulator drained (all four quarters loaded)
 constexpr int kBarRhoFull = kBarAccEmpty + 2;    // [4] per-unit row de-scale written
-constexpr int kBarMFull = kBarRhoFull + 4;       // [2] groups 1-3 partials staged for the merge
+constexpr int kBarMFull = kBarRhoFull + 4;       // [2] groups 1.. partials staged for the merge
 constexpr int kBarMEmpty = kBarMFull + 2;        // [2] group 0 consumed them
 constexpr int kBarMmaDone = kBarMEmpty + 2;      // all MMAs retired (teardown)
 constexpr int kBarCtabFull = kBarMmaDone + 1;    // [4] class table of a tile landed
@@ -190,7 +190,7 @@ struct RowState {
 // columns (shared-window addresses; warp-uniform, broadcast loads).
 //
 // First-argmax search: a quarter is searched only when its max beats the group's own best
-// AND reaches the row's threshold `rowmax` - the largest best any of the four groups has
+// AND reaches the row's threshold `rowmax` - the largest best any epilogue group has
 // published for this row in this unit (a 64-bit word: unit tag above, f32_ord(best) below;
 // a word with another tag counts as no threshold). The threshold never exceeds the unit's
 // true maximum, so the quarter that holds the first maximum is always searched, while the
@@ -374,8 +374,9 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackParams p) {
 //   warp 2      lane 0 (fused variant): class-table producer (TMA bulk copies, 4-slot ring)
 //   warp 3      idle
 //   warps 4-7   A converters: f32 rows -> (hi, lo) fp16 parts in TMEM, one lane quadrant each
-//   warps 8-23  epilogue groups 0-3 (4 warps each, lane quadrants 0-3); group g drains
-//               columns [32g, 32g+32) of every accumulator tile
+//   warps 8-31  epilogue groups 0-5 (4 warps each, lane quadrants 0-3); the 32-column
+//               quarters of the CTA's accumulator tiles, numbered in order, go round-robin
+//               to the groups: group g takes quarters g, g+6, g+12, ...
 template <bool EMIT_LOGITS, int NPOLY>
 __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_constant__ HeadParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -403,7 +404,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             mbar_init(bar(kBarAEmpty + i), 1);
             mbar_init(bar(kBarAccFull + i), 1);
             mbar_init(bar(kBarAccEmpty + i), 512);
-            mbar_init(bar(kBarMFull + i), 384);
+            mbar_init(bar(kBarMFull + i), 128 * (kEpiGroups - 1));
             mbar_init(bar(kBarMEmpty + i), 128);
         }
         for (int i = 0; i < 4; ++i) {
@@ -459,6 +460,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         // Whole warp, uniform control flow; elect.sync inside the issue sequences.
         const uint32_t idesc = idesc_f16_f32(128, 128);
         const int steps = p.hi_steps + p.lo_steps;
+        const bool k120 = p.hi_steps == 8 && p.lo_steps == 7 && p.merged_tail;  // K in 113..120
         // Per-step B descriptor offsets (16-byte units, added to the stage's descriptor).
         uint32_t boff[16];
 #pragma unroll
@@ -485,14 +487,18 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + kTmemAcc + buf * 128u;
                 const uint64_t bdesc0 = smem_desc_k_sw128(base + kOffB + (uint32_t)s * kTileBytes);
+                if (k120) {
+                    mma_tile_k120_warp(d_tmem, a_tmem, bdesc0, idesc, bar(kBarBEmpty + s), bar(kBarAccFull + (int)buf));
+                } else {
 #pragma unroll
-                for (int step = 0; step < 16; ++step) {
-                    if (step < steps)
-                        mma_f16_ts_warp(d_tmem, a_tmem + (uint32_t)step * 8u, bdesc0 + boff[step], idesc,
-                                        step > 0 ? 1u : 0u);
+                    for (int step = 0; step < 16; ++step) {
+                        if (step < steps)
+                            mma_f16_ts_warp(d_tmem, a_tmem + (uint32_t)step * 8u, bdesc0 + boff[step], idesc,
+                                            step > 0 ? 1u : 0u);
+                    }
+                    mma_commit_warp(bar(kBarBEmpty + s));
+                    mma_commit_warp(bar(kBarAccFull + (int)buf));
                 }
-                mma_commit_warp(bar(kBarBEmpty + s));
-                mma_commit_warp(bar(kBarAccFull + (int)buf));
             }
             if (!ok) break;
             mma_commit_warp(bar(kBarAEmpty + (int)ab));
@@ -580,17 +586,20 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         }
     } else if (warp >= 8) {
         // ------------------------------------------------------------- epilogue
-        // Group g owns columns [32g, 32g+32) of every accumulator tile: one 32-column TMEM load,
-        // the accumulator goes straight back to the MMA issuer, then the math runs from registers.
-        // Four groups give every SM sub-partition four independent warps of softmax work.
+        // Each quarter is one 32-column TMEM load; the accumulator goes back to the MMA
+        // issuer once its four quarters are loaded, and the math runs from registers. Six
+        // groups give every SM sub-partition six independent warps of softmax work; a group
+        // sees a different column subset of each row, which the online update and the merge
+        // at the end of the unit do not mind.
         const int g = (warp - 8) >> 2;
         const int q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        uint32_t cc = 0, uc = 0;
+        uint32_t cc0 = 0, uc = 0;  // tiles before this unit, units so far
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
             const Unit U = unit_of(u, p);
+            const uint32_t ntile = (uint32_t)(U.c1 - U.c0);
             const uint32_t slot = uc & 3u;
             const long long row = (long long)U.mb * kBlockM + r;
             RowState st{-CUDART_INF_F, 0.0f, -CUDART_INF_F, 0};
@@ -599,7 +608,13 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             if (!wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6)) break;
             const float rho = rho_s[slot * 128 + r];
             const bool scaled = qflag_s[slot * 4 + q] != 0u;
-            for (int c = U.c0; c < U.c1; ++c, ++cc) {
+            // this group's quarters of the unit: Q = 4*cc + k in [4*cc0, 4*(cc0+ntile)), Q % 6 == g
+            const uint32_t qb = 4u * cc0, qe = 4u * (cc0 + ntile);
+            uint32_t Q = qb + ((uint32_t)g + kEpiGroups - qb % kEpiGroups) % kEpiGroups;
+            bool first = true;
+            for (; Q < qe; Q += kEpiGroups) {
+                const uint32_t cc = Q >> 2, k = Q & 3u;
+                const int c = U.c0 + (int)(cc - cc0);
                 const uint32_t buf = cc & 1u;
                 const uint32_t cslot = cc % kCtabSlots;
                 if (!EMIT_LOGITS &&
@@ -613,10 +628,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 }
                 tc_fence_after();
                 uint32_t v[32];
-                tmem_ld32x32b_x32_wait(tmem + lane_base + kTmemAcc + buf * 128u + (uint32_t)(32 * g), v);
+                tmem_ld32x32b_x32_wait(tmem + lane_base + kTmemAcc + buf * 128u + 32u * k, v);
                 tc_fence_before();
                 mbar_arrive(bar(kBarAccEmpty + (int)buf));
-                const int col0 = c * kBlockN + 32 * g;
+                const int col0 = c * kBlockN + 32 * (int)k;
                 if (EMIT_LOGITS) {
                     const float2* cp = p.colp + (size_t)col0;
                     float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
@@ -625,8 +640,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                         else logits_quarter<false>(v, cp, col0, rho, out_row, p.n);
                     }
                 } else {
-                    const uint32_t cs = base + kOffCtab + cslot * kCtabBytes + 4u * (uint32_t)(32 * g);
-                    if (c == U.c0) {
+                    const uint32_t cs = base + kOffCtab + cslot * kCtabBytes + 4u * 32u * k;
+                    if (first) {
                         if (scaled)
                             fused_quarter<true, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
                         else
@@ -637,35 +652,38 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                         else
                             fused_quarter<false, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
                     }
+                    first = false;
                     mbar_arrive(bar(kBarCtabEmpty + (int)cslot));
                 }
             }
             if (!ok) break;
+            cc0 += ntile;
             if (!EMIT_LOGITS) {
-                // Merge the four groups' partial rows for this unit through shared memory.
+                // Merge the groups' partial rows for this unit through shared memory.
                 const uint32_t mb2 = uc & 1u;
-                float4* mg = merge_s + mb2 * 384;
+                float4* mg = merge_s + mb2 * (kEpiGroups - 1) * 128;
                 if (g != 0) {
                     if (!wait_bar(bar(kBarMEmpty + (int)mb2), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 8)) break;
                     mg[(g - 1) * 128 + r] = make_float4(st.off, st.sum, st.best, __int_as_float(st.idx));
                     mbar_arrive(bar(kBarMFull + (int)mb2));
                 } else {
                     if (!wait_bar(bar(kBarMFull + (int)mb2), (uc >> 1) & 1u, abort_flag, p, 9)) break;
-                    const float4 o1 = mg[r], o2 = mg[128 + r], o3 = mg[256 + r];
+                    float4 o[kEpiGroups - 1];
+#pragma unroll
+                    for (int j = 0; j < kEpiGroups - 1; ++j) o[j] = mg[j * 128 + r];
                     mbar_arrive(bar(kBarMEmpty + (int)mb2));
                     // Unit maximum = the largest offset; the argmax comes from the group(s)
                     // whose tracked best equals it (ties: lower class index).
-                    const float M = fmaxf(fmaxf(st.off, o1.x), fmaxf(o2.x, o3.x));
-                    float S = 0.0f;
-                    if (st.off != -CUDART_INF_F) S += st.sum * ex2_approx(st.off - M);
-                    if (o1.x != -CUDART_INF_F) S += o1.y * ex2_approx(o1.x - M);
-                    if (o2.x != -CUDART_INF_F) S += o2.y * ex2_approx(o2.x - M);
-                    if (o3.x != -CUDART_INF_F) S += o3.y * ex2_approx(o3.x - M);
-                    int I = 0x7fffffff;
-                    if (st.best == M) I = st.idx;
-                    if (o1.z == M) I = min(I, __float_as_int(o1.w));
-                    if (o2.z == M) I = min(I, __float_as_int(o2.w));
-                    if (o3.z == M) I = min(I, __float_as_int(o3.w));
+                    float M = st.off;
+#pragma unroll
+                    for (int j = 0; j < kEpiGroups - 1; ++j) M = fmaxf(M, o[j].x);
+                    float S = st.off != -CUDART_INF_F ? st.sum * ex2_approx(st.off - M) : 0.0f;
+                    int I = st.best == M ? st.idx : 0x7fffffff;
+#pragma unroll
+                    for (int j = 0; j < kEpiGroups - 1; ++j) {
+                        if (o[j].x != -CUDART_INF_F) S += o[j].y * ex2_approx(o[j].x - M);
+                        if (o[j].z == M) I = min(I, __float_as_int(o[j].w));
+                    }
                     if (I == 0x7fffffff) I = 0;  // no class at all (cannot happen for a real unit)
                     if (row < p.m) {
                         if (p.n_splits == 1) {
