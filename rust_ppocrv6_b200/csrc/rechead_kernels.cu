@@ -40,30 +40,37 @@ constexpr uint32_t kOffCtab = kOffMerge + 2 * (kEpiGroups - 1) * 128 * 16;  // [
 constexpr uint32_t kCtabSlots = 4;
 constexpr uint32_t kCtabBytes = 256 * 4;
 constexpr uint32_t kOffRowMax = kOffCtab + kCtabSlots * kCtabBytes;  // [128] u64 (unit tag, ordered max)
-constexpr uint32_t kSmemUsed = kOffRowMax + 128 * 8;
+constexpr uint32_t kOffAStage = kOffRowMax + 128 * 8;           // [128][k] f32 feature rows of a unit
+constexpr uint32_t kAStageBytes = kBlockM * kPadK * 4;
+constexpr uint32_t kSmemUsed = kOffAStage + kAStageBytes;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;               // + alignment slack
-static_assert(kOffCtab % 16 == 0, "bulk-copy destination alignment");
+static_assert(kOffCtab % 16 == 0 && kOffAStage % 16 == 0, "bulk-copy destination alignment");
+static_assert(kSmemUsed + 1024 <= 227 * 1024, "shared memory per CTA");
 
 // mbarrier indices
 constexpr int kBarBFull = 0;                     // [kStages] weight tile landed
 constexpr int kBarBEmpty = kBarBFull + kStages;  // [kStages] MMAs reading the tile done
-constexpr int kBarAFull = kBarBEmpty + kStages;  // [2] A operand written to TMEM
-constexpr int kBarAEmpty = kBarAFull + 2;        // [2] MMAs of the unit done with A
-constexpr int kBarAccFull = kBarAEmpty + 2;      // [2] accumulator ready
-constexpr int kBarAccEmpty = kBarAccFull + 2;    // [2] accumulator drained (all four quarters loaded)
-constexpr int kBarRhoFull = kBarAccEmpty + 2;    // [4] per-unit row de-scale written
+constexpr int kAccBufs = 3;                      // accumulator buffers in TMEM
+constexpr int kBarAFull = kBarBEmpty + kStages;  // A operand of the unit written to TMEM
+constexpr int kBarAEmpty = kBarAFull + 1;        // MMAs of the unit done with A
+constexpr int kBarAccFull = kBarAEmpty + 1;      // [kAccBufs] accumulator ready
+constexpr int kBarAccEmpty = kBarAccFull + kAccBufs;  // [kAccBufs] accumulator drained (four quarters loaded)
+constexpr int kBarRhoFull = kBarAccEmpty + kAccBufs;  // [4] per-unit row de-scale written
 constexpr int kBarMFull = kBarRhoFull + 4;       // [2] groups 1.. partials staged for the merge
 constexpr int kBarMEmpty = kBarMFull + 2;        // [2] group 0 consumed them
 constexpr int kBarMmaDone = kBarMEmpty + 2;      // all MMAs retired (teardown)
 constexpr int kBarCtabFull = kBarMmaDone + 1;    // [4] class table of a tile landed
 constexpr int kBarCtabEmpty = kBarCtabFull + 4;  // [4] all epilogue groups are done with it
-constexpr int kNumBars = kBarCtabEmpty + 4;
+constexpr int kBarStageFull = kBarCtabEmpty + 4;  // f32 feature rows of the next unit landed
+constexpr int kBarStageRead = kBarStageFull + 1;  // converters done reading the staged rows
+constexpr int kNumBars = kBarStageRead + 1;
 static_assert(kNumBars <= 48, "barrier area");
 
-// TMEM columns: A operand buffers [0,128) and [128,256), accumulators [256,384), [384,512).
+// TMEM columns: A operand [0,128) (hi and lo fp16 parts, 2 per column), accumulators
+// [128,256), [256,384), [384,512).
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = 0;
-constexpr uint32_t kTmemAcc = 256;
+constexpr uint32_t kTmemAcc = 128;
 
 constexpr uint32_t kSleepHintNs = 20000;  // longest a waiting thread stays suspended per try
 
@@ -399,11 +406,15 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             mbar_init(bar(kBarBFull + s), 1);
             mbar_init(bar(kBarBEmpty + s), 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(bar(kBarAFull + i), 128);
-            mbar_init(bar(kBarAEmpty + i), 1);
+        mbar_init(bar(kBarAFull), 128);
+        mbar_init(bar(kBarAEmpty), 1);
+        mbar_init(bar(kBarStageFull), 1);
+        mbar_init(bar(kBarStageRead), 128);
+        for (int i = 0; i < kAccBufs; ++i) {
             mbar_init(bar(kBarAccFull + i), 1);
             mbar_init(bar(kBarAccEmpty + i), 512);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(bar(kBarMFull + i), 128 * (kEpiGroups - 1));
             mbar_init(bar(kBarMEmpty + i), 128);
         }
@@ -472,16 +483,15 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
             const Unit U = unit_of(u, p);
-            const uint32_t ab = uc & 1u;
-            ok = __all_sync(0xffffffffu, wait_bar(bar(kBarAFull + ab), (uc >> 1) & 1u, abort_flag, p, 2));
+            ok = __all_sync(0xffffffffu, wait_bar(bar(kBarAFull), uc & 1u, abort_flag, p, 2));
             if (!ok) break;
             tc_fence_after();
-            const uint32_t a_tmem = tmem + kTmemA + ab * 128u;
+            const uint32_t a_tmem = tmem + kTmemA;
             for (int c = U.c0; c < U.c1; ++c, ++cc) {
                 const int s = (int)(cc % kStages);
-                const uint32_t buf = cc & 1u;
+                const uint32_t buf = cc % kAccBufs;
                 bool w = wait_bar(bar(kBarBFull + s), (cc / kStages) & 1u, abort_flag, p, 3);
-                w = w && wait_bar(bar(kBarAccEmpty + buf), ((cc >> 1) & 1u) ^ 1u, abort_flag, p, 4);
+                w = w && wait_bar(bar(kBarAccEmpty + (int)buf), ((cc / kAccBufs) & 1u) ^ 1u, abort_flag, p, 4);
                 ok = __all_sync(0xffffffffu, w);
                 if (!ok) break;
                 tc_fence_after();
@@ -501,7 +511,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 }
             }
             if (!ok) break;
-            mma_commit_warp(bar(kBarAEmpty + (int)ab));
+            mma_commit_warp(bar(kBarAEmpty));
         }
         mma_commit_warp(bar(kBarMmaDone));
         drain_bar(bar(kBarMmaDone), 0u, p);
@@ -537,18 +547,47 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         const int r = q * 32 + lane;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         const int steps = p.hi_steps + p.lo_steps;
+        // Fast path (the K = 113..120 layout with K % 4 == 0 and 16-byte aligned features): the
+        // 128 feature rows of the next unit are bulk-copied into shared memory while the current
+        // unit runs, so the A switch at a unit boundary is a shared-memory -> TMEM conversion.
+        const bool staged = p.hi_steps == 8 && p.lo_steps == 7 && p.merged_tail && (p.k % 4) == 0 &&
+                            ((reinterpret_cast<uintptr_t>(p.a) & 15u) == 0);
+        const float* stage_g = reinterpret_cast<const float*>(gbase + kOffAStage);
+        auto issue_stage = [&](int u) {  // one thread: rows of unit u -> staging buffer
+            const Unit V = unit_of(u, p);
+            const long long r0 = (long long)V.mb * kBlockM;
+            const long long nrows = min((long long)kBlockM, p.m - r0);
+            const uint32_t bytes = (uint32_t)(nrows * p.k * 4);
+            mbar_arrive_expect_tx(bar(kBarStageFull), bytes);
+            bulk_copy_g2s(base + kOffAStage, p.a + r0 * p.k, bytes, bar(kBarStageFull));
+        };
+        uint32_t staged_issued = 0, staged_used = 0;
+        if (staged && r == 0 && (int)blockIdx.x < units) {
+            issue_stage(blockIdx.x);
+            staged_issued = 1;
+        }
         uint32_t uc = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc) {
             const Unit U = unit_of(u, p);
-            const uint32_t ab = uc & 1u, slot = uc & 3u;
-            if (!wait_bar(bar(kBarAEmpty + (int)ab), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 5)) break;
-            tc_fence_after();
+            const uint32_t slot = uc & 3u;
             const long long row = (long long)U.mb * kBlockM + r;
             const bool valid = row < p.m;
-            const float* arow = p.a + (valid ? row : 0) * (long long)p.k;
+            const float* arow = staged ? stage_g + (size_t)r * p.k : p.a + (valid ? row : 0) * (long long)p.k;
+            if (staged) {
+                if (!wait_bar(bar(kBarStageFull), uc & 1u, abort_flag, p, 12)) break;
+                staged_used = uc + 1;
+            }
             float max_abs = 0.0f;
-            if (valid)
-                for (int kk = 0; kk < p.k; ++kk) max_abs = fmaxf(max_abs, fabsf(__ldg(arow + kk)));
+            if (valid) {
+                if (staged) {
+                    for (int kk = 0; kk < p.k; kk += 4) {
+                        const float4 x = lds128(smem_u32(arow + kk));
+                        max_abs = fmaxf(max_abs, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+                    }
+                } else {
+                    for (int kk = 0; kk < p.k; ++kk) max_abs = fmaxf(max_abs, fabsf(__ldg(arow + kk)));
+                }
+            }
             // fp16 holds the parts only below 65504: rows with max|a| >= 2^14 are scaled by a
             // power of two (exact) into [2^14, 2^15) and de-scaled in the epilogue.
             float rs = 1.0f, rho = 1.0f;
@@ -558,32 +597,82 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 rho = __uint_as_float((uint32_t)(127 + e - 14) << 23);
             }
             const uint32_t need = __ballot_sync(0xffffffffu, rs != 1.0f);
-            for (int g4 = 0; g4 * 4 < steps; ++g4) {
-                uint32_t wv[32];
+            if (!wait_bar(bar(kBarAEmpty), (uc & 1u) ^ 1u, abort_flag, p, 5)) break;
+            tc_fence_after();
+            const uint32_t a_t = tmem + lane_base + kTmemA;
+            if (staged) {
+                // pair p (K slots 2p, 2p+1): hi part -> column p; lo part -> column 64 + p
+                // (p < 56) or 4 + p (p = 56..59, the merged tail).
+#pragma unroll 1
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t hw[8], lw[8];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int step = g4 * 4 + t;
-#pragma unroll
-                    for (int w = 0; w < 8; ++w) {
-                        uint32_t packed = 0u;
-                        if (step < steps) {
-                            const __half lo_h = a_part(arow, valid, p.k, rs, step, 2 * w, p.hi_steps, p.merged_tail);
-                            const __half hi_h =
-                                a_part(arow, valid, p.k, rs, step, 2 * w + 1, p.hi_steps, p.merged_tail);
-                            packed = (uint32_t)__half_as_ushort(lo_h) | ((uint32_t)__half_as_ushort(hi_h) << 16);
+                    for (int h = 0; h < 2; ++h) {
+                        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+                        const int kk = 16 * j + 8 * h;
+                        if (valid && kk < p.k) {
+                            x0 = lds128(smem_u32(arow + kk));
+                            if (kk + 4 < p.k) x1 = lds128(smem_u32(arow + kk + 4));
                         }
-                        wv[t * 8 + w] = packed;
+                        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            const float a0 = xs[2 * w] * rs, a1 = xs[2 * w + 1] * rs;
+                            const __half2 hv = __floats2half2_rn(a0, a1);
+                            const float2 hf = __half22float2(hv);
+                            const __half2 lv = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+                            hw[4 * h + w] = *reinterpret_cast<const uint32_t*>(&hv);
+                            lw[4 * h + w] = *reinterpret_cast<const uint32_t*>(&lv);
+                        }
+                    }
+                    if (j < 7) {
+                        tmem_st32x32b_x8(a_t + 8u * j, hw);
+                        tmem_st32x32b_x8(a_t + 64u + 8u * j, lw);
+                    } else {
+                        const uint32_t h4[4] = {hw[0], hw[1], hw[2], hw[3]};
+                        const uint32_t l4[4] = {lw[0], lw[1], lw[2], lw[3]};
+                        tmem_st32x32b_x4(a_t + 56u, h4);
+                        tmem_st32x32b_x4(a_t + 60u, l4);
                     }
                 }
-                tmem_st32x32b_x32(tmem + lane_base + kTmemA + ab * 128u + (uint32_t)g4 * 32u, wv);
+                mbar_arrive(bar(kBarStageRead));
+            } else {
+                for (int g4 = 0; g4 * 4 < steps; ++g4) {
+                    uint32_t wv[32];
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const int step = g4 * 4 + t;
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) {
+                            uint32_t packed = 0u;
+                            if (step < steps) {
+                                const __half lo_h =
+                                    a_part(arow, valid, p.k, rs, step, 2 * w, p.hi_steps, p.merged_tail);
+                                const __half hi_h =
+                                    a_part(arow, valid, p.k, rs, step, 2 * w + 1, p.hi_steps, p.merged_tail);
+                                packed = (uint32_t)__half_as_ushort(lo_h) | ((uint32_t)__half_as_ushort(hi_h) << 16);
+                            }
+                            wv[t * 8 + w] = packed;
+                        }
+                    }
+                    tmem_st32x32b_x32(a_t + (uint32_t)g4 * 32u, wv);
+                }
             }
             tmem_st_wait();
             rho_s[slot * 128 + r] = rho;
             if (lane == 0) qflag_s[slot * 4 + q] = need;
             tc_fence_before();
-            mbar_arrive(bar(kBarAFull + (int)ab));
+            mbar_arrive(bar(kBarAFull));
             mbar_arrive(bar(kBarRhoFull + (int)slot));
+            // next unit's rows into the staging buffer once every converter has read this one
+            if (staged && r == 0 && u + (int)gridDim.x < units) {
+                if (!wait_bar(bar(kBarStageRead), uc & 1u, abort_flag, p, 13)) break;
+                issue_stage(u + (int)gridDim.x);
+                ++staged_issued;
+            }
         }
+        // a staged copy still in flight must land before the CTA exits
+        if (staged && r == 0 && staged_issued > staged_used) drain_bar(bar(kBarStageFull), (staged_issued - 1) & 1u, p);
     } else if (warp >= 8) {
         // ------------------------------------------------------------- epilogue
         // Each quarter is one 32-column TMEM load; the accumulator goes back to the MMA
@@ -615,14 +704,14 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             for (; Q < qe; Q += kEpiGroups) {
                 const uint32_t cc = Q >> 2, k = Q & 3u;
                 const int c = U.c0 + (int)(cc - cc0);
-                const uint32_t buf = cc & 1u;
+                const uint32_t buf = cc % kAccBufs;
                 const uint32_t cslot = cc % kCtabSlots;
                 if (!EMIT_LOGITS &&
                     !wait_bar(bar(kBarCtabFull + (int)cslot), (cc / kCtabSlots) & 1u, abort_flag, p, 11)) {
                     ok = false;
                     break;
                 }
-                if (!wait_bar(bar(kBarAccFull + (int)buf), (cc >> 1) & 1u, abort_flag, p, 7)) {
+                if (!wait_bar(bar(kBarAccFull + (int)buf), (cc / kAccBufs) & 1u, abort_flag, p, 7)) {
                     ok = false;
                     break;
                 }
