@@ -236,7 +236,9 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
     // The offset is known before this quarter (FIRST: qmax), so the exps need not wait for
     // the max tree of the other branch and both run interleaved.
     const float2 nm = make_float2(-st.off, -st.off);
-    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+    // One pairwise sum chain: its latency hides behind the other warps, and a second chain
+    // measured slower (more live registers and instructions).
+    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
         const float2 x = __fadd2_rn(make_float2(t[i], t[i + 1]), nm);
@@ -245,12 +247,8 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
             e = exp2_poly2(x);
         else
             e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-        if ((i >> 1) & 1)
-            acc1 = __fadd2_rn(acc1, e);
-        else
-            acc0 = __fadd2_rn(acc0, e);
+        acc = __fadd2_rn(acc, e);
     }
-    const float2 acc = __fadd2_rn(acc0, acc1);
     float sq = acc.x + acc.y;
     if constexpr (FIRST) {
         st.sum = sq;
