@@ -179,22 +179,34 @@ __device__ __forceinline__ uint32_t f32_ord(float x) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+// Inverse of f32_ord.
+__device__ __forceinline__ float ord_f32(uint32_t o) {
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
 // Per-row state of one epilogue group over a work unit.
-//   off, sum : sum = sum of 2^(t - off) over every column seen; off = their max.
+//   off, sum : sum = sum of 2^(t - off) over every column seen. off = 0 is the absolute
+//              mode, kept while the row's max lies in [kAbsLo, kAbsHi]: there 2^t neither
+//              overflows (18,816 terms <= 2^115) nor loses a term that matters (those below
+//              2^-126 are < 2^-66 of the max), so no per-column offset is subtracted.
+//              Otherwise off is the running max and the sum is rescaled when it rises.
 //   best, idx: max and first argmax over the columns whose quarter reached the row's shared
 //              threshold (see fused_quarter); the group that holds the unit's maximum always
 //              tracks it, so the unit's (max, argmax) is the best of the groups' (best, idx).
+//   thr      : last value of the shared threshold this thread read (never above it).
 struct RowState {
     float off, sum, best;
     int idx;
+    float thr;
 };
+constexpr float kAbsLo = -60.0f, kAbsHi = 100.0f;
 
 // 32 accumulator columns of one row: t = D*c + e (the logit in log2 units), then the online
-// update of `st`. The exps are taken relative to the running max from before these columns
-// (so they need not wait for this quarter's max); the sum is rescaled once if the max rose,
-// and recomputed exactly in the rare case that it rose by more than 64 (2^64 bounds every
-// term, so nothing overflows). `cs`/`es` are the shared-memory class table entries of these
-// columns (shared-window addresses; warp-uniform, broadcast loads).
+// update of `st`. In the relative mode the exps are taken against the running max from
+// before these columns (so they need not wait for this quarter's max); the sum is rescaled
+// once if the max rose, and recomputed exactly in the rare case that it rose by more than 64
+// (2^64 bounds every term, so nothing overflows). `cs`/`es` are the shared-memory class
+// table entries of these columns (shared-window addresses; warp-uniform, broadcast loads).
 //
 // First-argmax search: a quarter is searched only when its max beats the group's own best
 // AND reaches the row's threshold `rowmax` - the largest best any epilogue group has
@@ -229,45 +241,60 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
     r1[10] = fmaxf(t[30], t[31]);
     const float qmax = max3f(max3f(r1[0], r1[1], r1[2]), max3f(r1[3], r1[4], r1[5]),
                              max3f(max3f(r1[6], r1[7], r1[8]), r1[9], r1[10]));
-    if constexpr (FIRST) {  // first columns of this row in the unit: offset = their max
+    if constexpr (FIRST) {  // first columns of this row in the unit: pick the mode
         if (qmax == -CUDART_INF_F) return;  // padded classes only
-        st.off = qmax;
+        st.off = (qmax >= kAbsLo && qmax <= kAbsHi) ? 0.0f : qmax;
     }
-    // The offset is known before this quarter (FIRST: qmax), so the exps need not wait for
-    // the max tree of the other branch and both run interleaved.
-    const float2 nm = make_float2(-st.off, -st.off);
-    // One pairwise sum chain: its latency hides behind the other warps, and a second chain
-    // measured slower (more live registers and instructions).
+    // The offset is known before this quarter, so the exps need not wait for the max tree
+    // and both run interleaved. A warp whose rows are all in the absolute mode skips the
+    // per-column subtraction.
     float2 acc = make_float2(0.f, 0.f);
+    if (__all_sync(0xffffffffu, st.off == 0.0f)) {
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-        const float2 x = __fadd2_rn(make_float2(t[i], t[i + 1]), nm);
-        float2 e;
-        if ((i >> 1) < NPOLY)
-            e = exp2_poly2(x);
-        else
-            e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-        acc = __fadd2_rn(acc, e);
+        for (int i = 0; i < 32; i += 2) {
+            const float2 x = make_float2(t[i], t[i + 1]);
+            float2 e;
+            if ((i >> 1) < NPOLY)
+                e = exp2_poly2(x);
+            else
+                e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            acc = __fadd2_rn(acc, e);
+        }
+    } else {
+        const float2 nm = make_float2(-st.off, -st.off);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+            const float2 x = __fadd2_rn(make_float2(t[i], t[i + 1]), nm);
+            float2 e;
+            if ((i >> 1) < NPOLY)
+                e = exp2_poly2(x);
+            else
+                e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            acc = __fadd2_rn(acc, e);
+        }
     }
     float sq = acc.x + acc.y;
-    if constexpr (FIRST) {
+    // absolute mode: leave it only if the max passes kAbsHi; relative mode: rescale on a rise
+    const float lim = st.off == 0.0f ? kAbsHi : st.off;
+    if (FIRST && st.off == 0.0f) {
         st.sum = sq;
-    } else if (qmax > st.off) {
+    } else if (qmax > lim) {
         if (qmax - st.off > 64.0f) {  // exact recompute relative to the new max
             sq = 0.0f;
 #pragma unroll
             for (int i = 0; i < 32; ++i) sq += ex2_approx(t[i] - qmax);
-            st.sum = (st.off == -CUDART_INF_F ? 0.0f : st.sum * ex2_approx(st.off - qmax)) + sq;
+            st.sum = (st.off == -CUDART_INF_F || FIRST ? 0.0f : st.sum * ex2_approx(st.off - qmax)) + sq;
         } else {
-            st.sum = (st.sum + sq) * ex2_approx(st.off - qmax);
+            st.sum = ((FIRST ? 0.0f : st.sum) + sq) * ex2_approx(st.off - qmax);
         }
         st.off = qmax;
     } else {
-        st.sum += sq;
+        st.sum = (FIRST ? 0.0f : st.sum) + sq;
     }
-    if (qmax > st.best) {
+    if (qmax > st.best && qmax >= st.thr) {
         const unsigned long long w = lds_u64(rowmax);
         const uint32_t thr = (uint32_t)(w >> 32) == tag ? (uint32_t)w : 0u;
+        st.thr = thr ? ord_f32(thr) : -CUDART_INF_F;
         const uint32_t qo = f32_ord(qmax);
         if (qo >= thr) {
             int first = 31;
@@ -689,7 +716,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             const uint32_t ntile = (uint32_t)(U.c1 - U.c0);
             const uint32_t slot = uc & 3u;
             const long long row = (long long)U.mb * kBlockM + r;
-            RowState st{-CUDART_INF_F, 0.0f, -CUDART_INF_F, 0};
+            RowState st{-CUDART_INF_F, 0.0f, -CUDART_INF_F, 0, -CUDART_INF_F};
             const uint32_t tag = uc + 1u;  // row thresholds of earlier units carry smaller tags
             const uint32_t rowmax = base + kOffRowMax + 8u * (uint32_t)r;
             if (!wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6)) break;
@@ -759,11 +786,12 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
 #pragma unroll
                     for (int j = 0; j < kEpiGroups - 1; ++j) o[j] = mg[j * 128 + r];
                     mbar_arrive(bar(kBarMEmpty + (int)mb2));
-                    // Unit maximum = the largest offset; the argmax comes from the group(s)
-                    // whose tracked best equals it (ties: lower class index).
-                    float M = st.off;
+                    // Unit maximum = the largest tracked best (the group holding the maximum
+                    // always tracks it); the argmax comes from the group(s) whose best equals
+                    // it (ties: lower class index); each sum is rescaled from its own offset.
+                    float M = st.best;
 #pragma unroll
-                    for (int j = 0; j < kEpiGroups - 1; ++j) M = fmaxf(M, o[j].x);
+                    for (int j = 0; j < kEpiGroups - 1; ++j) M = fmaxf(M, o[j].z);
                     float S = st.off != -CUDART_INF_F ? st.sum * ex2_approx(st.off - M) : 0.0f;
                     int I = st.best == M ? st.idx : 0x7fffffff;
 #pragma unroll
