@@ -253,6 +253,76 @@ def test_fused_cfg4_precision_stress(rh, ctx, oracle):
     assert np.all(ref["gap"][wl.tie_rows] < 1.2e-4)  # the construction did build near-ties
 
 
+def _extreme_weights(n=2000, k=120, seed=21):
+    rng = np.random.default_rng(seed)
+    w = (0.05 * rng.standard_normal((n, k))).astype(np.float32)
+    w[1700] = w[300]  # an identical class in another tile (and another epilogue group)
+    return w
+
+
+@pytest.mark.parametrize("case", ["mode_switch", "all_very_negative", "huge_rows", "mixed_warps"])
+def test_fused_extreme_logit_ranges(rh, ctx, oracle, case):
+    """Rows whose maximum leaves the absolute-exp range mid-unit (a class with bias +80,
+    ~115 in log2 units), rows entirely below it (every bias -200), rows far above it
+    (features x 1e3 and x 1e5, the latter on the power-of-two rescaled path), and warps that
+    mix such rows with ordinary ones."""
+    n, k, m = 2000, 120, 256
+    rng = np.random.default_rng(22)
+    w = _extreme_weights(n, k)
+    bias = (0.01 * rng.standard_normal(n)).astype(np.float32)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    if case == "mode_switch":
+        bias[1500] = 80.0
+        x *= 20.0  # spread the logits so the probabilities are not all ~1
+    elif case == "all_very_negative":
+        bias[:] = -200.0 + bias
+    elif case == "huge_rows":
+        x[: m // 2] *= 1e3
+        x[m // 2:] *= 1e5
+    else:  # mixed_warps: every 4th row huge (relative mode) among ordinary rows (absolute mode)
+        x[::4] *= 1e3
+        bias[1500] = 80.0
+    qw, q, s = pack_both(rh, ctx, oracle, w, bias)
+    off = np.array([0, m], np.int64)
+    idx, prob = rh.head_decode(x, qw, line_offsets=off)
+    ref = oracle.head_decode(x, off, q, s, bias, threads=8, want_gap=True)
+    mism = idx != ref["idx"]
+    assert np.all(ref["gap"][mism] < TIE_GAP), f"[{case}] argmax differs beyond a near-tie"
+    # At logit magnitudes L of 100s, f32 itself moves every logit difference by ~ulp(L), so the
+    # probability bar is the one the logits bar implies: 1e-5 + 2 x (2e-6 relative) x |L|.
+    lmax = np.abs(oracle.matmul_quantized_b(x, q, s, bias)).max(axis=1)
+    tol = PROB_REL_TOL + 2 * LOGIT_REL_TOL * lmax
+    rel = np.abs(prob.astype(np.float64) - ref["prob"]) / ref["prob"]
+    assert np.all(rel[~mism] <= tol[~mism]), f"[{case}] max prob rel err {rel[~mism].max():.3g}"
+
+
+def test_fused_exact_ties_take_the_first_index(rh, ctx, oracle):
+    """Exact logit ties across tiles and epilogue groups: the lower class index wins, as
+    find_argmax (src/postprocess/ctc.rs:178) returns the first maximum."""
+    n, k, m = 2000, 120, 192
+    w = _extreme_weights(n, k)
+    bias = np.zeros(n, np.float32)
+    bias[300] = bias[1700] = 5.0  # classes 300 and 1700 are identical and on top
+    x = np.random.default_rng(23).standard_normal((m, k), dtype=np.float32)
+    x[: m // 3] = 0.0  # all logits equal 0 except the two biased classes
+    qw, q, s = pack_both(rh, ctx, oracle, w, bias)
+    off = np.array([0, m], np.int64)
+    idx, prob = rh.head_decode(x, qw, line_offsets=off)
+    ref = oracle.head_decode(x, off, q, s, bias, threads=8, want_gap=True)
+    logits = oracle.matmul_quantized_b(x, q, s, bias)
+    top = logits.max(axis=1)
+    first = np.argmax(logits == top[:, None], axis=1)
+    exact = (logits == top[:, None]).sum(axis=1) > 1  # rows with an exact tie in the oracle
+    assert exact[: m // 3].all()
+    np.testing.assert_array_equal(idx[exact], first[exact])
+    np.testing.assert_array_equal(idx[: m // 3], 300)
+    assert_fused(idx, prob, ref, "ties")
+    z = np.zeros((m, k), np.float32)
+    idx0, prob0 = rh.head_decode(z, rh.QuantizedWeight.from_f32_transposed(w, ctx=ctx), line_offsets=off)
+    np.testing.assert_array_equal(idx0, 0)  # every logit 0: the first class
+    np.testing.assert_allclose(prob0, 1.0 / n, rtol=1e-5)
+
+
 @pytest.mark.parametrize("pairs", ["0", "2", "4", "6", "8"])
 def test_fused_every_exp_offload_setting(rh, ctx, oracle, monkeypatch, pairs):
     """Each instantiation of the epilogue (0-8 exp pairs of every 64 on the FMA-pipe
