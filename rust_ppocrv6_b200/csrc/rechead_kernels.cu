@@ -407,8 +407,8 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackParams p) {
 //   warp 3      idle
 //   warps 4-7   A converters: f32 rows -> (hi, lo) fp16 parts in TMEM, one lane quadrant each
 //   warps 8-31  epilogue groups 0-5 (4 warps each, lane quadrants 0-3); the 32-column
-//               quarters of the CTA's accumulator tiles, numbered in order, go round-robin
-//               to the groups: group g takes quarters g, g+6, g+12, ...
+//               quarters of a unit's accumulator tiles, numbered in order from the unit's
+//               start, go round-robin to the groups: group g takes quarters g, g+6, ...
 template <bool EMIT_LOGITS, int NPOLY>
 __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_constant__ HeadParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -722,13 +722,14 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             if (!wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6)) break;
             const float rho = rho_s[slot * 128 + r];
             const bool scaled = qflag_s[slot * 4 + q] != 0u;
-            // this group's quarters of the unit: Q = 4*cc + k in [4*cc0, 4*(cc0+ntile)), Q % 6 == g
-            const uint32_t qb = 4u * cc0, qe = 4u * (cc0 + ntile);
-            uint32_t Q = qb + ((uint32_t)g + kEpiGroups - qb % kEpiGroups) % kEpiGroups;
+            // this group's quarters of the unit: Q = 4*(tile within the unit) + k, Q % 6 == g
+            // (numbered from each unit's start, so a row's summation order depends only on
+            // its unit's tile range, not on which CTA runs the unit or what it ran before)
+            const uint32_t qe = 4u * ntile;
             bool first = true;
-            for (; Q < qe; Q += kEpiGroups) {
-                const uint32_t cc = Q >> 2, k = Q & 3u;
-                const int c = U.c0 + (int)(cc - cc0);
+            for (uint32_t Q = (uint32_t)g; Q < qe; Q += kEpiGroups) {
+                const uint32_t cc = cc0 + (Q >> 2), k = Q & 3u;
+                const int c = U.c0 + (int)(Q >> 2);
                 const uint32_t buf = cc % kAccBufs;
                 const uint32_t cslot = cc % kCtabSlots;
                 if (!EMIT_LOGITS &&

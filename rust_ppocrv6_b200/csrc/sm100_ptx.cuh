@@ -56,7 +56,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 
 // ------------------------------------------------------------- TMA bulk copy
 // Untiled bulk copy global -> this CTA's shared memory; completion is signalled on `bar`
-// as transaction bytes. Both addresses 16-byte aligned, size a multiple of 16. No multicast.
+// as transaction bytes. Both addresses 16-byte aligned, size a multiple of 16; this CTA only.
 __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),

@@ -487,8 +487,11 @@ def test_multi_device_shards_and_redispatch(rh, oracle, monkeypatch):
             qw1 = rh.QuantizedWeight.from_f32_transposed(wl.w_t, ctx=c1, bias=wl.bias)
             idx1, prob1 = rh.head_decode(wl.x, qw1, line_offsets=wl.line_offsets)
             qw1.free()
-        assert np.array_equal(idx, idx1) and np.array_equal(prob, prob1)
+        # shards get their own class-range split plans, so sums may differ in the last bits
+        assert np.array_equal(idx, idx1)
+        np.testing.assert_allclose(prob, prob1, rtol=2e-6)
         monkeypatch.setenv("RH_FAULT_DEVICE", "1")
         idx2, prob2 = rh.head_decode(wl.x, qw, line_offsets=wl.line_offsets)
-        assert np.array_equal(idx2, idx1) and np.array_equal(prob2, prob1)
+        # the failed shard is redone on device 0 with the same plan: identical results
+        assert np.array_equal(idx2, idx) and np.array_equal(prob2, prob)
         qw.free()
