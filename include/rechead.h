@@ -177,6 +177,34 @@ int64_t rh_launch_count(const rh_ctx *ctx, int slot);
 int64_t rh_ctc_collapse(const int32_t *idx, const float *prob, const int64_t *line_offsets, int64_t n_lines,
                         int32_t *tokens, int64_t *token_offsets, float *scores);
 
+/*
+ * rh_ctc_collapse on the GPU, device memory, on context device `slot` and `stream`
+ * (cudaStream_t, NULL = the legacy default stream): the same rule and the same outputs
+ * (d_tokens back to back, d_token_offsets with n_lines + 1 entries starting at 0, d_scores
+ * bit-identical to the host loop) for (d_idx, d_prob) that rh_head_decode_device left on
+ * the device. Replaces the collapse loop of CtcDecoder::decode_batch
+ * (src/postprocess/ctc.rs:144-169) after a GPU head. d_line_offsets index d_idx/d_prob
+ * (non-decreasing; a decreasing pair counts as an empty line); d_tokens needs room for
+ * d_line_offsets[n_lines] - d_line_offsets[0] entries. Asynchronous: three kernel launches.
+ */
+int rh_ctc_collapse_device(rh_ctx *ctx, int slot, const int32_t *d_idx, const float *d_prob,
+                           const int64_t *d_line_offsets, int64_t n_lines, int32_t *d_tokens, int64_t *d_token_offsets,
+                           float *d_scores, void *stream);
+
+/*
+ * The whole recognition head of a batch of text lines with the collapse on the GPU:
+ * rh_head_decode_lines (sharded over the context's devices) followed by
+ * rh_ctc_collapse_device on each shard, so only the collapsed tokens and one score per line
+ * leave the GPUs. Outputs as rh_ctc_collapse (host memory; tokens needs room for
+ * line_offsets[n_lines] - line_offsets[0] entries). Replaces the per-line
+ * matmul_quantized_b -> softmax_inplace -> CtcDecoder::decode chain of
+ * OcrEngine::recognize (src/pipeline.rs:364-436, src/postprocess/ctc.rs:103-175) for this
+ * head; text = the vocabulary entries of the tokens (CtcDecoder::decode_indices in the
+ * binding). Same errors as rh_head_decode_lines.
+ */
+int rh_head_decode_ctc(rh_ctx *ctx, const rh_weight *w, const float *a, const int64_t *line_offsets, int64_t n_lines,
+                       int64_t k, int32_t *tokens, int64_t *token_offsets, float *scores);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,8 @@ SIGNATURES = {
     "rh_sync": (_c_int, [_vp, _c_int]),
     "rh_launch_count": (_c_i64, [_vp, _c_int]),
     "rh_ctc_collapse": (_c_i64, [_vp, _vp, _vp, _c_i64, _vp, _vp, _vp]),
+    "rh_ctc_collapse_device": (_c_int, [_vp, _c_int, _vp, _vp, _vp, _c_i64, _vp, _vp, _vp, _vp]),
+    "rh_head_decode_ctc": (_c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _vp, _vp, _vp]),
 }
 
 _lib = None

@@ -69,6 +69,9 @@ cudaError_t launch_pack(const PackParams& p, cudaStream_t stream);
 cudaError_t launch_head(const HeadParams& p, bool emit_logits, int grid, cudaStream_t stream);
 cudaError_t launch_merge(const float4* partial, int n_splits, long long m, int32_t* idx, float* prob,
                          cudaStream_t stream);
+// CTC greedy collapse of per-timestep (idx, prob) in device memory (ctc_kernels.cu).
+cudaError_t launch_ctc_collapse(const int32_t* idx, const float* prob, const int64_t* line_offsets, int64_t n_lines,
+                                int32_t* tokens, int64_t* token_offsets, float* scores, cudaStream_t stream);
 size_t head_smem_bytes();
 cudaError_t head_kernel_setup();
 

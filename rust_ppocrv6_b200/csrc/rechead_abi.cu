@@ -59,6 +59,7 @@ struct Slot {
     cudaEvent_t copied = nullptr;
     int* d_status = nullptr;
     DevBuf a, idx, prob, out, partial;
+    DevBuf lines, tok_off, tokens, scores;  // CTC collapse on the device
     std::mutex mu;
     int64_t launches = 0;
 };
@@ -215,11 +216,10 @@ const rh_weight::Per* weight_on(const rh_weight* w, int device) {
 }
 
 // Host-memory head on one slot: H2D rows, kernels, D2H results, synchronise, check status.
-int run_host_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, int64_t rows, int32_t* idx,
+// The host-memory pass on one device; the caller holds s.mu. With idx == prob == logits ==
+// nullptr the per-timestep (idx, prob) stay in s.idx / s.prob for a following device step.
+int host_pass_locked(rh_ctx* ctx, const rh_weight* w, Slot& s, const float* a, int64_t rows, int32_t* idx,
                      float* prob, float* logits) {
-    if (rows <= 0) return RH_OK;
-    Slot& s = *ctx->slots[slot];
-    std::lock_guard<std::mutex> lock(s.mu);
     RH_CUDA(cudaSetDevice(s.device));
     const rh_weight::Per* pw = weight_on(w, s.device);
     if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
@@ -251,14 +251,64 @@ int run_host_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, 
             int rc = enqueue_head(ctx, w, s, *pw, dst, n, (int32_t*)s.idx.p + r0, (float*)s.prob.p + r0, nullptr,
                                   false, s.stream);
             if (rc) return rc;
-            RH_CUDA(cudaMemcpyAsync(idx + r0, (int32_t*)s.idx.p + r0, (size_t)n * sizeof(int32_t),
-                                    cudaMemcpyDeviceToHost, s.stream));
-            RH_CUDA(cudaMemcpyAsync(prob + r0, (float*)s.prob.p + r0, (size_t)n * sizeof(float),
-                                    cudaMemcpyDeviceToHost, s.stream));
+            if (idx) {
+                RH_CUDA(cudaMemcpyAsync(idx + r0, (int32_t*)s.idx.p + r0, (size_t)n * sizeof(int32_t),
+                                        cudaMemcpyDeviceToHost, s.stream));
+                RH_CUDA(cudaMemcpyAsync(prob + r0, (float*)s.prob.p + r0, (size_t)n * sizeof(float),
+                                        cudaMemcpyDeviceToHost, s.stream));
+            }
         }
     }
+    return RH_OK;
+}
+
+int run_host_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, int64_t rows, int32_t* idx,
+                     float* prob, float* logits) {
+    if (rows <= 0) return RH_OK;
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    if (int rc = host_pass_locked(ctx, w, s, a, rows, idx, prob, logits)) return rc;
     RH_CUDA(cudaStreamSynchronize(s.stream));
     return read_status(s);
+}
+
+// The fused head then the CTC collapse on one device for lines [0, n_lines) of a shard whose
+// rows start at a (line_offsets rebased so that line_offsets[0] == 0). tokens receives the
+// shard's tokens back to back, token_offsets its n_lines + 1 offsets (from 0), scores one per
+// line. Only the collapsed result comes back to the host.
+int run_ctc_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, const int64_t* line_offsets,
+                    int64_t n_lines, int32_t* tokens, int64_t* token_offsets, float* scores) {
+    const int64_t rows = line_offsets[n_lines];
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    if (rows > 0) {
+        if (int rc = host_pass_locked(ctx, w, s, a, rows, nullptr, nullptr, nullptr)) return rc;
+    } else {
+        RH_CUDA(cudaSetDevice(s.device));
+        RH_CUDA(s.idx.ensure(sizeof(int32_t)));
+        RH_CUDA(s.prob.ensure(sizeof(float)));
+    }
+    const size_t off_bytes = (size_t)(n_lines + 1) * sizeof(int64_t);
+    RH_CUDA(s.lines.ensure(off_bytes));
+    RH_CUDA(s.tok_off.ensure(off_bytes));
+    RH_CUDA(s.tokens.ensure((size_t)std::max<int64_t>(rows, 1) * sizeof(int32_t)));
+    RH_CUDA(s.scores.ensure((size_t)std::max<int64_t>(n_lines, 1) * sizeof(float)));
+    RH_CUDA(cudaMemcpyAsync(s.lines.p, line_offsets, off_bytes, cudaMemcpyHostToDevice, s.stream));
+    RH_CUDA(rh::launch_ctc_collapse((const int32_t*)s.idx.p, (const float*)s.prob.p, (const int64_t*)s.lines.p, n_lines,
+                                    (int32_t*)s.tokens.p, (int64_t*)s.tok_off.p, (float*)s.scores.p, s.stream));
+    s.launches += n_lines > 0 ? 3 : 1;
+    RH_CUDA(cudaMemcpyAsync(token_offsets, s.tok_off.p, off_bytes, cudaMemcpyDeviceToHost, s.stream));
+    if (n_lines > 0)
+        RH_CUDA(cudaMemcpyAsync(scores, s.scores.p, (size_t)n_lines * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    if (int rc = read_status(s)) return rc;
+    const int64_t n_tok = token_offsets[n_lines];
+    if (n_tok < 0 || n_tok > rows) return fail(RH_ERR_CUDA, "CTC collapse produced an impossible token count");
+    if (n_tok > 0) {
+        RH_CUDA(cudaMemcpyAsync(tokens, s.tokens.p, (size_t)n_tok * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
+        RH_CUDA(cudaStreamSynchronize(s.stream));
+    }
+    return RH_OK;
 }
 
 int upload_colp(rh_ctx* ctx, rh_weight* w, const float* bias) {
@@ -715,6 +765,106 @@ int64_t rh_ctc_collapse(const int32_t* idx, const float* prob, const int64_t* li
     return w;
 }
 
+
+int rh_ctc_collapse_device(rh_ctx* ctx, int slot, const int32_t* d_idx, const float* d_prob,
+                           const int64_t* d_line_offsets, int64_t n_lines, int32_t* d_tokens, int64_t* d_token_offsets,
+                           float* d_scores, void* stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (slot < 0 || slot >= (int)ctx->slots.size()) return fail(RH_ERR_INVALID_ARG, "slot out of range");
+    if (n_lines < 0) return fail(RH_ERR_INVALID_ARG, "negative line count");
+    if (!d_token_offsets) return fail(RH_ERR_INVALID_ARG, "null device pointer");
+    if (n_lines > 0 && (!d_idx || !d_prob || !d_line_offsets || !d_tokens || !d_scores))
+        return fail(RH_ERR_INVALID_ARG, "null device pointer");
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    RH_CUDA(rh::launch_ctc_collapse(d_idx, d_prob, d_line_offsets, n_lines, d_tokens, d_token_offsets, d_scores,
+                                    (cudaStream_t)stream));
+    s.launches += n_lines > 0 ? 3 : 1;
+    return RH_OK;
+}
+
+int rh_head_decode_ctc(rh_ctx* ctx, const rh_weight* w, const float* a, const int64_t* line_offsets, int64_t n_lines,
+                       int64_t k, int32_t* tokens, int64_t* token_offsets, float* scores) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (k != w->k)
+        return fail(RH_ERR_INVALID_ARG,
+                    "Inner dimensions must match: " + std::to_string(k) + " != " + std::to_string(w->k));
+    if (n_lines < 0 || !line_offsets || !token_offsets) return fail(RH_ERR_INVALID_ARG, "bad line offsets");
+    if (line_offsets[0] < 0) return fail(RH_ERR_INVALID_ARG, "line offsets must start at >= 0");
+    for (int64_t l = 0; l < n_lines; ++l)
+        if (line_offsets[l + 1] < line_offsets[l]) return fail(RH_ERR_INVALID_ARG, "line offsets must not decrease");
+    token_offsets[0] = 0;
+    if (n_lines == 0) return RH_OK;
+    const int64_t r0 = line_offsets[0], total = line_offsets[n_lines] - r0;
+    if (!scores || (total > 0 && (!a || !tokens))) return fail(RH_ERR_INVALID_ARG, "null input or output");
+
+    // Contiguous line shards with balanced timestep counts, one per device (as in
+    // rh_head_decode_lines); shard d writes its tokens at its own row range of `tokens`, and
+    // the shards are packed back to back once all have finished.
+    const int nd = (int)ctx->slots.size();
+    std::vector<int64_t> lcut(nd + 1, 0);
+    lcut[nd] = n_lines;
+    for (int d = 1; d < nd; ++d) {
+        const int64_t target = r0 + (total * d) / nd;
+        int64_t l = lcut[d - 1];
+        while (l < n_lines && line_offsets[l] < target) ++l;
+        lcut[d] = l;
+    }
+    const std::vector<int> faults = injected_fault_slots();
+    std::vector<int> rc(nd, RH_OK);
+    std::vector<std::string> msg(nd);
+    std::vector<std::vector<int64_t>> local_off(nd);
+    auto run = [&](int d, int on_slot) {
+        const int64_t l0 = lcut[d], l1 = lcut[d + 1];
+        if (l1 <= l0) return;
+        if (std::find(faults.begin(), faults.end(), on_slot) != faults.end()) {
+            rc[d] = RH_ERR_DEVICE_FAULT;
+            msg[d] = "injected failure on slot " + std::to_string(on_slot);
+            return;
+        }
+        std::vector<int64_t> lo(l1 - l0 + 1);
+        for (int64_t l = l0; l <= l1; ++l) lo[l - l0] = line_offsets[l] - line_offsets[l0];
+        local_off[d].assign(l1 - l0 + 1, 0);
+        rc[d] = run_ctc_on_slot(ctx, w, on_slot, a + (size_t)(line_offsets[l0] - r0) * (size_t)k, lo.data(), l1 - l0,
+                                tokens + (line_offsets[l0] - r0), local_off[d].data(), scores + l0);
+        if (rc[d]) msg[d] = g_err;
+    };
+    if (nd == 1) {
+        run(0, 0);
+    } else {
+        std::vector<std::thread> th;
+        for (int d = 0; d < nd; ++d) th.emplace_back(run, d, d);
+        for (auto& t : th) t.join();
+    }
+    int healthy = -1;
+    for (int d = 0; d < nd; ++d)
+        if (rc[d] == RH_OK && std::find(faults.begin(), faults.end(), d) == faults.end()) {
+            healthy = d;
+            break;
+        }
+    for (int d = 0; d < nd; ++d) {
+        if (rc[d] == RH_OK) continue;
+        if (rc[d] == RH_ERR_INVALID_ARG) return fail(rc[d], msg[d]);
+        if (healthy < 0) return fail(RH_ERR_DEVICE_FAULT, "every device shard failed; last: " + msg[d]);
+        run(d, healthy);
+        if (rc[d] != RH_OK) return fail(rc[d], msg[d]);
+    }
+    // pack the shards' tokens back to back (each shard's tokens sit at the start of its rows)
+    int64_t wpos = 0;
+    for (int d = 0; d < nd; ++d) {
+        const int64_t l0 = lcut[d], l1 = lcut[d + 1];
+        if (l1 <= l0) continue;
+        const int64_t n_tok = local_off[d][l1 - l0];
+        const int64_t src = line_offsets[l0] - r0;
+        if (n_tok > 0 && src != wpos) std::memmove(tokens + wpos, tokens + src, (size_t)n_tok * sizeof(int32_t));
+        for (int64_t l = l0; l < l1; ++l) token_offsets[l] = wpos + local_off[d][l - l0];
+        wpos += n_tok;
+    }
+    token_offsets[n_lines] = wpos;
+    return RH_OK;
+}
 
 int rh_head_decode_device_noalloc(rh_ctx* ctx, const rh_weight* w, int slot, const float* d_a, int64_t rows,
                                   int32_t* d_idx, float* d_prob, void* stream) {

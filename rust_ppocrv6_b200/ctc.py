@@ -1,7 +1,8 @@
 """CtcDecoder mirror (src/postprocess/ctc.rs) that consumes the fused head's per-timestep
 (argmax index, max probability) instead of the [batch, time, vocab] probability tensor.
 
-The collapse itself runs in librechead.so (rh_ctc_collapse, host code, no device needed).
+The collapse itself runs in librechead.so: rh_ctc_collapse on the host (no device needed), or
+rh_ctc_collapse_device / rh_head_decode_ctc on the GPU.
 """
 from __future__ import annotations
 
@@ -74,6 +75,21 @@ class CtcDecoder:
             if t.size and (t.max() >= len(self.vocab) or t.min() < 0):
                 raise RecHeadError(RH_ERR_INVALID_ARG, "class index outside the dictionary")
             out.append(("".join(self.vocab[i] for i in t), float(s)))
+        return out
+
+    def decode_lines(self, a, qw, line_offsets):
+        """The whole head of a line batch with the collapse on the GPU (rh_head_decode_ctc):
+        decode_batch's [(text, score)] per line straight from the SVTR features."""
+        from .head import head_decode_ctc
+
+        self.check_classes(qw.rows)
+        tokens, toff, scores = head_decode_ctc(a, qw, line_offsets)
+        out = []
+        for l in range(toff.size - 1):
+            t = tokens[toff[l]:toff[l + 1]]
+            if t.size and (t.max() >= len(self.vocab) or t.min() < 0):
+                raise RecHeadError(RH_ERR_INVALID_ARG, "class index outside the dictionary")
+            out.append(("".join(self.vocab[i] for i in t), float(scores[l])))
         return out
 
     def decode(self, idx, prob, n_classes: int | None = None):

@@ -233,6 +233,34 @@ def head_decode(a, qw: QuantizedWeight, bias=None, line_offsets=None):
     return idx.reshape(lead), prob.reshape(lead)
 
 
+def head_decode_ctc(a, qw: QuantizedWeight, line_offsets, bias=None):
+    """The head of a line batch with the CTC collapse on the GPU (rh_head_decode_ctc):
+    returns (tokens int32 [total], token_offsets int64 [n_lines + 1], scores f32 [n_lines]),
+    the outputs of rh_ctc_collapse, with only those leaving the GPUs."""
+    a = _f32(a)
+    lead, rows = _rows(a, qw.cols)
+    if bias is not None:
+        _use_bias(qw, bias)
+    off = np.ascontiguousarray(line_offsets, dtype=np.int64)
+    if off.size < 1 or off[0] != 0 or off[-1] != rows:
+        raise RecHeadError(RH_ERR_INVALID_ARG, "line_offsets must run from 0 to the row count")
+    n_lines = off.size - 1
+    tokens = np.empty(max(rows, 1), np.int32)
+    toff = np.empty(n_lines + 1, np.int64)
+    scores = np.empty(max(n_lines, 1), np.float32)
+    check(load().rh_head_decode_ctc(qw._ctx.handle, qw.handle, _p(a), _p(off), n_lines, qw.cols, _p(tokens),
+                                    _p(toff), _p(scores)))
+    return tokens[:toff[-1]].copy(), toff, scores[:n_lines].copy()
+
+
+def ctc_collapse_device(ctx: Context, idx_ptr: int, prob_ptr: int, offsets_ptr: int, n_lines: int, tokens_ptr: int,
+                        token_offsets_ptr: int, scores_ptr: int, stream: int = 0, slot: int = 0) -> None:
+    """rh_ctc_collapse_device on raw CUDA pointers (e.g. torch tensors' data_ptr())."""
+    vp = ctypes.c_void_p
+    check(load().rh_ctc_collapse_device(ctx.handle, slot, vp(idx_ptr), vp(prob_ptr), vp(offsets_ptr), n_lines,
+                                        vp(tokens_ptr), vp(token_offsets_ptr), vp(scores_ptr), vp(stream or None)))
+
+
 def head_decode_device(qw: QuantizedWeight, a_ptr: int, rows: int, idx_ptr: int, prob_ptr: int, stream: int = 0,
                        slot: int = 0) -> None:
     """Device-memory fused head (raw CUDA pointers, e.g. torch tensors' data_ptr()) on `stream`."""

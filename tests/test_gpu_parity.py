@@ -475,6 +475,72 @@ def test_ctc_decode_from_fused_head(rh, ctx, oracle):
             assert abs(sc - s_ref) <= 1e-5 * max(s_ref, 1e-30)
 
 
+def _collapse_inputs(seed=31):
+    """Per-timestep (idx, prob) with blanks and repeats, and line lengths around the warp
+    width (0, 1, 31, 32, 33, 64, 65, ...), starting at a non-zero row."""
+    rng = np.random.default_rng(seed)
+    lens = [0, 1, 2, 31, 32, 33, 0, 64, 65, 120, 7, 200, 0, 0, 97, 3, 128, 129, 5, 1]
+    lens += list(rng.integers(0, 150, size=300))
+    start = 5
+    off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64) + start
+    total = int(off[-1]) + 4
+    idx = rng.integers(0, 6, size=total).astype(np.int32)  # small alphabet: many repeats
+    idx[rng.random(total) < 0.3] = 0  # blanks
+    big = rng.random(total) < 0.1
+    idx[big] = rng.integers(6, 18710, size=int(big.sum()))
+    prob = rng.random(total).astype(np.float32)
+    return idx, prob, off
+
+
+def test_ctc_collapse_on_device_is_bit_identical_to_host(rh, ctx, oracle):
+    import torch
+
+    idx, prob, off = _collapse_inputs()
+    n_lines = off.size - 1
+    dev = torch.device("cuda", 0)
+    d_idx, d_prob, d_off = (torch.from_numpy(v).to(dev) for v in (idx, prob, off))
+    d_tok = torch.full((int(off[-1] - off[0]),), -1, dtype=torch.int32, device=dev)
+    d_toff = torch.full((n_lines + 1,), -1, dtype=torch.int64, device=dev)
+    d_sc = torch.full((n_lines,), -1.0, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    rh.ctc_collapse_device(ctx, d_idx.data_ptr(), d_prob.data_ptr(), d_off.data_ptr(), n_lines, d_tok.data_ptr(),
+                           d_toff.data_ptr(), d_sc.data_ptr())
+    ctx.sync()
+    toff = d_toff.cpu().numpy()
+    tok = d_tok.cpu().numpy()[:toff[-1]]
+    sc = d_sc.cpu().numpy()
+    ref_t, ref_s = oracle.ctc_collapse(idx, prob, off)
+    np.testing.assert_array_equal(toff, np.concatenate([[0], np.cumsum([t.size for t in ref_t])]))
+    np.testing.assert_array_equal(tok, np.concatenate(ref_t))
+    np.testing.assert_array_equal(sc.view(np.uint32), ref_s.view(np.uint32))  # bit-identical scores
+    host_t, host_s = rh.CtcDecoder([]).collapse(idx, prob, off)
+    np.testing.assert_array_equal(np.concatenate(host_t), tok)
+    np.testing.assert_array_equal(host_s.view(np.uint32), sc.view(np.uint32))
+
+
+def test_head_decode_ctc_equals_head_then_host_collapse(rh, ctx, oracle):
+    """rh_head_decode_ctc (head + collapse on the GPU, only tokens and scores come back)
+    against rh_head_decode_lines + the host collapse, and against the oracle's decode."""
+    from rust_ppocrv6_b200 import workloads
+
+    wl = workloads.make(1)
+    qw, q, s = pack_both(rh, ctx, oracle, wl.w_t, wl.bias)
+    tokens, toff, scores = rh.head_decode_ctc(wl.x, qw, wl.line_offsets)
+    idx, prob = rh.head_decode(wl.x, qw, line_offsets=wl.line_offsets)
+    ht, hs = rh.CtcDecoder([]).collapse(idx, prob, wl.line_offsets)
+    np.testing.assert_array_equal(toff, np.concatenate([[0], np.cumsum([t.size for t in ht])]))
+    np.testing.assert_array_equal(tokens, np.concatenate(ht))
+    np.testing.assert_array_equal(scores.view(np.uint32), hs.view(np.uint32))
+    dec = rh.CtcDecoder.from_vocab(["blank"] + [f"c{i}" for i in range(1, workloads.N - 1)] + [" "])
+    lines = dec.decode_lines(wl.x, qw, wl.line_offsets)
+    assert lines == dec.decode_indices(idx, prob, wl.line_offsets, n_classes=workloads.N)
+    ref = oracle.head_decode(wl.x, wl.line_offsets, q, s, wl.bias, threads=8, want_gap=True)
+    assert_fused(idx, prob, ref, "ctc-gpu")
+    # empty batches and all-empty lines
+    t0, o0, s0 = rh.head_decode_ctc(np.zeros((0, workloads.K), np.float32), qw, np.array([0, 0, 0]))
+    assert t0.size == 0 and o0.tolist() == [0, 0, 0] and s0.tolist() == [0.0, 0.0]
+
+
 @pytest.mark.skipif("__import__('torch').cuda.device_count() < 2")
 def test_multi_device_shards_and_redispatch(rh, oracle, monkeypatch):
     from rust_ppocrv6_b200 import workloads
