@@ -32,9 +32,15 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-K_DIM = 120
-N_CLASSES = 18710
-FLOP_PER_ROW = 2 * K_DIM * N_CLASSES  # algorithmic FLOPs per timestep (2*K*N)
+K_DIM = 120        # SVTR features per timestep (the small model's head; --workload tiny: 80)
+N_CLASSES = 18710  # CTC classes (--workload tiny: 6906)
+
+
+def head_dims(workload: str):
+    """(K, N) of the head the workload runs."""
+    from rust_ppocrv6_b200 import workloads
+
+    return (workloads.K_TINY, workloads.N_TINY) if workload == "tiny" else (K_DIM, N_CLASSES)
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "W8A32 rec-head decoded timesteps/s (MatMul.12+Add.204 -> Softmax.2 -> argmax)"
 UNIT = "timesteps/s"
@@ -46,7 +52,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "tiny"], default="cfg2")
     ap.add_argument("--cpu-sample-lines", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -67,6 +73,11 @@ def workload_for(name: str, world: int, rank: int):
         off = workloads.uniform_offsets(1024, 120)
         desc = f"cfg2: 1024 lines x T=120 per GPU (M=122880/GPU), K=120, N=18710; global batch {1024 * world} lines"
         return off, int(off[-1]), int(off[-1]) * world, desc, "weak"
+    if name == "tiny":
+        off = workloads.uniform_offsets(1024, 120)
+        desc = (f"cfg5 (tiny model head): 1024 lines x T=120 per GPU (M=122880/GPU), K=80, N=6906; "
+                f"global batch {1024 * world} lines")
+        return off, int(off[-1]), int(off[-1]) * world, desc, "weak"
     rng = np.random.default_rng(workloads.SEED + 3)
     off_all = workloads.ragged_offsets(rng, 8192)
     l0, l1 = workloads.shard_lines(off_all, world, rank)
@@ -75,16 +86,17 @@ def workload_for(name: str, world: int, rank: int):
     return off, int(off[-1]), int(off_all[-1]), desc, "strong"
 
 
-def synth(rows: int, seed: int):
+def synth(rows: int, seed: int, k: int = K_DIM):
     rng = np.random.default_rng(seed)
-    return rng.standard_normal((rows, K_DIM), dtype=np.float32)
+    return rng.standard_normal((rows, k), dtype=np.float32)
 
 
-def head_weights():
+def head_weights(workload: str = "cfg2"):
     from rust_ppocrv6_b200 import workloads
 
+    k, n = head_dims(workload)
     rng = np.random.default_rng(workloads.SEED + 2)
-    return workloads.head_weights(rng)
+    return workloads.head_weights(rng, n=n, k=k)
 
 
 class ClockSampler:
@@ -192,8 +204,8 @@ def run_reference_arm(args, world, rank):
     if rank != 0:
         return
     off, rows, _, desc, _ = workload_for(args.workload, 1, 0)
-    w_t, bias = head_weights()
-    x = synth(min(rows, int(off[min(args.cpu_sample_lines, off.size - 1)])), 1234)
+    w_t, bias = head_weights(args.workload)
+    x = synth(min(rows, int(off[min(args.cpu_sample_lines, off.size - 1)])), 1234, w_t.shape[1])
     from oracle import oracle
 
     q, s = oracle.pack(w_t)
@@ -253,11 +265,12 @@ def main():
         return float(t.item())
 
     off, rows, global_rows, desc, scaling = workload_for(args.workload, world, rank)
-    w_t, bias = head_weights()
+    w_t, bias = head_weights(args.workload)
+    k_dim, n_classes = w_t.shape[1], w_t.shape[0]
     ctx = rh.Context(devices=[local])
     qw = rh.QuantizedWeight.from_f32_transposed(w_t, ctx=ctx, bias=bias)
 
-    x_host = synth(rows, 1000 + rank)
+    x_host = synth(rows, 1000 + rank, k_dim)
     x_bytes = x_host.nbytes
     n_copies = max(2, int(np.ceil(2 * L2_BYTES / max(x_bytes, 1))) + 1)
     n_copies = min(n_copies, 64)
@@ -304,7 +317,7 @@ def main():
     lib = rh.load()
 
     def e2e_step():
-        rh._lib.check(lib.rh_head_decode(ctx.handle, qw.handle, ctypes.c_void_p(x_pin.data_ptr()), rows, K_DIM,
+        rh._lib.check(lib.rh_head_decode(ctx.handle, qw.handle, ctypes.c_void_p(x_pin.data_ptr()), rows, k_dim,
                                          ctypes.c_void_p(idx_h.data_ptr()), ctypes.c_void_p(prob_h.data_ptr())))
 
     for _ in range(max(3, args.warmup)):
@@ -319,7 +332,7 @@ def main():
 
     # roofline of the dominant kernel (the fused head; the split merge is <1 % of a step)
     peak, peak_src = measured_peak_tflops()
-    achieved = FLOP_PER_ROW * rows / (dev_ms / args.steps / 1e3) / 1e12
+    achieved = 2 * k_dim * n_classes * rows / (dev_ms / args.steps / 1e3) / 1e12  # 2*K*N per timestep
     traffic = profiled_traffic()
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "peak_source": peak_src,

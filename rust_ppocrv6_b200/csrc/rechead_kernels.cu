@@ -497,6 +497,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         const uint32_t idesc = idesc_f16_f32(128, 128);
         const int steps = p.hi_steps + p.lo_steps;
         const bool k120 = p.hi_steps == 8 && p.lo_steps == 7 && p.merged_tail;  // K in 113..120
+        const bool k80 = p.hi_steps == 5 && p.lo_steps == 5 && !p.merged_tail;  // K in 73..80
         // Per-step B descriptor offsets (16-byte units, added to the stage's descriptor).
         uint32_t boff[16];
 #pragma unroll
@@ -524,6 +525,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 const uint64_t bdesc0 = smem_desc_k_sw128(base + kOffB + (uint32_t)s * kTileBytes);
                 if (k120) {
                     mma_tile_k120_warp(d_tmem, a_tmem, bdesc0, idesc, bar(kBarBEmpty + s), bar(kBarAccFull + (int)buf));
+                } else if (k80) {
+                    mma_tile_k80_warp(d_tmem, a_tmem, bdesc0, idesc, bar(kBarBEmpty + s), bar(kBarAccFull + (int)buf));
                 } else {
 #pragma unroll
                     for (int step = 0; step < 16; ++step) {
@@ -572,11 +575,14 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         const int r = q * 32 + lane;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         const int steps = p.hi_steps + p.lo_steps;
-        // Fast path (the K = 113..120 layout with K % 4 == 0 and 16-byte aligned features): the
-        // 128 feature rows of the next unit are bulk-copied into shared memory while the current
-        // unit runs, so the A switch at a unit boundary is a shared-memory -> TMEM conversion.
-        const bool staged = p.hi_steps == 8 && p.lo_steps == 7 && p.merged_tail && (p.k % 4) == 0 &&
+        // Fast path (K % 4 == 0, 16-byte aligned features, and either the merged-tail layout of
+        // K = 113..120 or a layout without a merged tail): the 128 feature rows of the next unit
+        // are bulk-copied into shared memory while the current unit runs, so the A switch at a
+        // unit boundary is a shared-memory -> TMEM conversion.
+        const bool merged120 = p.hi_steps == 8 && p.lo_steps == 7 && p.merged_tail;
+        const bool staged = (merged120 || (!p.merged_tail && p.lo_steps == p.hi_steps)) && (p.k % 4) == 0 &&
                             ((reinterpret_cast<uintptr_t>(p.a) & 15u) == 0);
+        const uint32_t lo_col = 8u * (uint32_t)p.hi_steps;  // first TMEM column of the low part
         const float* stage_g = reinterpret_cast<const float*>(gbase + kOffAStage);
         auto issue_stage = [&](int u) {  // one thread: rows of unit u -> staging buffer
             const Unit V = unit_of(u, p);
@@ -626,10 +632,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             tc_fence_after();
             const uint32_t a_t = tmem + lane_base + kTmemA;
             if (staged) {
-                // pair p (K slots 2p, 2p+1): hi part -> column p; lo part -> column 64 + p
-                // (p < 56) or 4 + p (p = 56..59, the merged tail).
+                // pair p (K slots 2p, 2p+1): hi part -> column p; lo part -> column 8*hi_steps + p,
+                // except the merged tail of K = 113..120 (p = 56..59 -> columns 60..63).
 #pragma unroll 1
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < p.hi_steps; ++j) {
                     uint32_t hw[8], lw[8];
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
@@ -650,9 +656,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                             lw[4 * h + w] = *reinterpret_cast<const uint32_t*>(&lv);
                         }
                     }
-                    if (j < 7) {
+                    if (!merged120 || j < 7) {
                         tmem_st32x32b_x8(a_t + 8u * j, hw);
-                        tmem_st32x32b_x8(a_t + 64u + 8u * j, lw);
+                        tmem_st32x32b_x8(a_t + lo_col + 8u * j, lw);
                     } else {
                         const uint32_t h4[4] = {hw[0], hw[1], hw[2], hw[3]};
                         const uint32_t l4[4] = {lw[0], lw[1], lw[2], lw[3]};

@@ -185,6 +185,51 @@ __device__ __forceinline__ void mma_tile_k120_warp(uint32_t d_tmem, uint32_t a_t
         : "memory");
 }
 
+// The same for the K = 73..80 layout of the tiny recognition model's head (5 high-part and
+// 5 low-part K-steps, no merged tail: 10 MMAs).
+__device__ __forceinline__ void mma_tile_k80_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                   uint32_t bar_b_empty, uint32_t bar_acc_full) {
+    asm volatile(
+        "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 b<10>;\n\t.reg .b32 a<10>;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 pf, 0, 0;\n\t"
+        "setp.eq.b32 pt, 0, 0;\n\t"
+        "add.s64 b0, %2, 0;\n\t"
+        "add.u32 a0, %1, 0;\n\t"
+        "add.s64 b1, %2, 2;\n\t"
+        "add.u32 a1, %1, 8;\n\t"
+        "add.s64 b2, %2, 4;\n\t"
+        "add.u32 a2, %1, 16;\n\t"
+        "add.s64 b3, %2, 6;\n\t"
+        "add.u32 a3, %1, 24;\n\t"
+        "add.s64 b4, %2, 1024;\n\t"
+        "add.u32 a4, %1, 32;\n\t"
+        "add.s64 b5, %2, 0;\n\t"
+        "add.u32 a5, %1, 40;\n\t"
+        "add.s64 b6, %2, 2;\n\t"
+        "add.u32 a6, %1, 48;\n\t"
+        "add.s64 b7, %2, 4;\n\t"
+        "add.u32 a7, %1, 56;\n\t"
+        "add.s64 b8, %2, 6;\n\t"
+        "add.u32 a8, %1, 64;\n\t"
+        "add.s64 b9, %2, 1024;\n\t"
+        "add.u32 a9, %1, 72;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], b0, %3, pf;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], b4, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], b5, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], b6, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], b7, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a8], b8, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a9], b9, %3, pt;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%4];\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(bar_b_empty), "r"(bar_acc_full)
+        : "memory");
+}
+
 // 1 for exactly one lane of the (converged) warp.
 __device__ __forceinline__ bool elect_one() {
     uint32_t e;

@@ -11,6 +11,8 @@ config, 0.05 * Student-t(3); biases N(0, 0.01^2) (real head: std 0.015).
   cfg3  8192 ragged lines, T ~ U{10..120}       M ~ 532k      (multi-GPU sharding)
   cfg4  256 lines x T=240, Student-t weights,   M = 61,440
         5 % of timesteps built as near-ties (top-2 logits within 1e-4)
+  cfg5  the tiny recognition model's head (linear_1.w_0, K=80 -> N=6906),
+        1024 lines x T=120                      M = 122,880
 """
 from __future__ import annotations
 
@@ -20,6 +22,8 @@ import numpy as np
 
 K = 120
 N = 18710
+K_TINY = 80
+N_TINY = 6906
 SEED = 0x5EED
 
 
@@ -103,10 +107,11 @@ def make_near_ties(rng, x: np.ndarray, rows: np.ndarray, w_deq: np.ndarray, bias
 
 
 def make(cfg: int, scale: float = 1.0, seed: int = SEED) -> Workload:
-    """Config `cfg` (0-4). `scale` < 1 shrinks the number of lines (test-sized variants)."""
+    """Config `cfg` (0-5). `scale` < 1 shrinks the number of lines (test-sized variants)."""
     rng = np.random.default_rng(seed + cfg)
     student = cfg == 4
-    w_t, bias = head_weights(rng, student_t=student)
+    n, k = (N_TINY, K_TINY) if cfg == 5 else (N, K)
+    w_t, bias = head_weights(rng, n=n, k=k, student_t=student)
     if cfg == 0:
         off = uniform_offsets(1, 120)
     elif cfg == 1:
@@ -117,10 +122,12 @@ def make(cfg: int, scale: float = 1.0, seed: int = SEED) -> Workload:
         off = ragged_offsets(rng, max(1, int(round(8192 * scale))))
     elif cfg == 4:
         off = uniform_offsets(max(1, int(round(256 * scale))), 240)
+    elif cfg == 5:
+        off = uniform_offsets(max(1, int(round(1024 * scale))), 120)
     else:
         raise ValueError(f"unknown config {cfg}")
     m = int(off[-1])
-    x = rng.standard_normal((m, K), dtype=np.float32)
+    x = rng.standard_normal((m, k), dtype=np.float32)
     tie_rows = np.zeros(0, np.int64)
     if cfg == 4:
         tie_rows = np.sort(rng.choice(m, size=max(1, m // 20), replace=False))

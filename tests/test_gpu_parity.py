@@ -244,6 +244,19 @@ def test_fused_cfg2_page_batch_subset(rh, ctx, oracle):
     fused_case(rh, ctx, oracle, workloads.make(2, scale=96 / 1024), "cfg2/96")
 
 
+def test_fused_tiny_model_head(rh, ctx, oracle):
+    """The tiny recognition model's head (K = 80 -> N = 6906, linear_1.w_0's shape): its own
+    fast paths (10-MMA issue sequence, staged features without a merged tail)."""
+    from rust_ppocrv6_b200 import workloads
+
+    wl = workloads.make(5, scale=24 / 1024)
+    assert wl.w_t.shape == (workloads.N_TINY, workloads.K_TINY)
+    fused_case(rh, ctx, oracle, wl, "cfg5/24")
+    qw, q, s = pack_both(rh, ctx, oracle, wl.w_t, wl.bias)
+    assert_logits_close(rh.matmul_quantized_b(wl.x[:300], qw, wl.bias),
+                        oracle.matmul_quantized_b(wl.x[:300], q, s, wl.bias))
+
+
 def test_fused_cfg4_precision_stress(rh, ctx, oracle):
     """Student-t weights (row outliers stretch the scales) and 5 % constructed near-ties."""
     from rust_ppocrv6_b200 import workloads
