@@ -242,8 +242,8 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
     const float qmax = max3f(max3f(r1[0], r1[1], r1[2]), max3f(r1[3], r1[4], r1[5]),
                              max3f(max3f(r1[6], r1[7], r1[8]), r1[9], r1[10]));
     if constexpr (FIRST) {  // first columns of this row in the unit: pick the mode
-        if (qmax == -CUDART_INF_F) return;  // padded classes only
-        st.off = (qmax >= kAbsLo && qmax <= kAbsHi) ? 0.0f : qmax;
+        // (no early return for padded-only columns: every lane reaches the warp votes below)
+        st.off = qmax == -CUDART_INF_F ? -CUDART_INF_F : (qmax >= kAbsLo && qmax <= kAbsHi) ? 0.0f : qmax;
     }
     // The offset is known before this quarter, so the exps need not wait for the max tree
     // and both run interleaved. A warp whose rows are all in the absolute mode skips the
@@ -276,7 +276,9 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
     float sq = acc.x + acc.y;
     // absolute mode: leave it only if the max passes kAbsHi; relative mode: rescale on a rise
     const float lim = st.off == 0.0f ? kAbsHi : st.off;
-    if (FIRST && st.off == 0.0f) {
+    if (FIRST && st.off == -CUDART_INF_F) {
+        st.sum = 0.0f;  // padded classes only: nothing to add
+    } else if (FIRST && st.off == 0.0f) {
         st.sum = sq;
     } else if (qmax > lim) {
         if (qmax - st.off > 64.0f) {  // exact recompute relative to the new max
@@ -605,7 +607,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             const bool valid = row < p.m;
             const float* arow = staged ? stage_g + (size_t)r * p.k : p.a + (valid ? row : 0) * (long long)p.k;
             if (staged) {
-                if (!wait_bar(bar(kBarStageFull), uc & 1u, abort_flag, p, 12)) break;
+                if (!__all_sync(0xffffffffu, wait_bar(bar(kBarStageFull), uc & 1u, abort_flag, p, 12))) break;
                 staged_used = uc + 1;
             }
             float max_abs = 0.0f;
@@ -628,7 +630,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 rho = __uint_as_float((uint32_t)(127 + e - 14) << 23);
             }
             const uint32_t need = __ballot_sync(0xffffffffu, rs != 1.0f);
-            if (!wait_bar(bar(kBarAEmpty), (uc & 1u) ^ 1u, abort_flag, p, 5)) break;
+            if (!__all_sync(0xffffffffu, wait_bar(bar(kBarAEmpty), (uc & 1u) ^ 1u, abort_flag, p, 5))) break;
             tc_fence_after();
             const uint32_t a_t = tmem + lane_base + kTmemA;
             if (staged) {
@@ -696,11 +698,16 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             mbar_arrive(bar(kBarAFull));
             mbar_arrive(bar(kBarRhoFull + (int)slot));
             // next unit's rows into the staging buffer once every converter has read this one
+            bool stop = false;
             if (staged && r == 0 && u + (int)gridDim.x < units) {
-                if (!wait_bar(bar(kBarStageRead), uc & 1u, abort_flag, p, 13)) break;
-                issue_stage(u + (int)gridDim.x);
-                ++staged_issued;
+                if (wait_bar(bar(kBarStageRead), uc & 1u, abort_flag, p, 13)) {
+                    issue_stage(u + (int)gridDim.x);
+                    ++staged_issued;
+                } else {
+                    stop = true;
+                }
             }
+            if (__any_sync(0xffffffffu, stop)) break;  // leave the loop as a whole warp
         }
         // a staged copy still in flight must land before the CTA exits
         if (staged && r == 0 && staged_issued > staged_used) drain_bar(bar(kBarStageFull), (staged_issued - 1) & 1u, p);
@@ -725,7 +732,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             RowState st{-CUDART_INF_F, 0.0f, -CUDART_INF_F, 0, -CUDART_INF_F};
             const uint32_t tag = uc + 1u;  // row thresholds of earlier units carry smaller tags
             const uint32_t rowmax = base + kOffRowMax + 8u * (uint32_t)r;
-            if (!wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6)) break;
+            if (!__all_sync(0xffffffffu, wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6))) break;
             const float rho = rho_s[slot * 128 + r];
             const bool scaled = qflag_s[slot * 4 + q] != 0u;
             // this group's quarters of the unit: Q = 4*(tile within the unit) + k, Q % 6 == g
@@ -739,11 +746,12 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 const uint32_t buf = cc % kAccBufs;
                 const uint32_t cslot = cc % kCtabSlots;
                 if (!EMIT_LOGITS &&
-                    !wait_bar(bar(kBarCtabFull + (int)cslot), (cc / kCtabSlots) & 1u, abort_flag, p, 11)) {
+                    !__all_sync(0xffffffffu,
+                                wait_bar(bar(kBarCtabFull + (int)cslot), (cc / kCtabSlots) & 1u, abort_flag, p, 11))) {
                     ok = false;
                     break;
                 }
-                if (!wait_bar(bar(kBarAccFull + (int)buf), (cc / kAccBufs) & 1u, abort_flag, p, 7)) {
+                if (!__all_sync(0xffffffffu, wait_bar(bar(kBarAccFull + (int)buf), (cc / kAccBufs) & 1u, abort_flag, p, 7))) {
                     ok = false;
                     break;
                 }
@@ -784,11 +792,12 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                 const uint32_t mb2 = uc & 1u;
                 float4* mg = merge_s + mb2 * (kEpiGroups - 1) * 128;
                 if (g != 0) {
-                    if (!wait_bar(bar(kBarMEmpty + (int)mb2), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 8)) break;
+                    if (!__all_sync(0xffffffffu, wait_bar(bar(kBarMEmpty + (int)mb2), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 8)))
+                        break;
                     mg[(g - 1) * 128 + r] = make_float4(st.off, st.sum, st.best, __int_as_float(st.idx));
                     mbar_arrive(bar(kBarMFull + (int)mb2));
                 } else {
-                    if (!wait_bar(bar(kBarMFull + (int)mb2), (uc >> 1) & 1u, abort_flag, p, 9)) break;
+                    if (!__all_sync(0xffffffffu, wait_bar(bar(kBarMFull + (int)mb2), (uc >> 1) & 1u, abort_flag, p, 9))) break;
                     float4 o[kEpiGroups - 1];
 #pragma unroll
                     for (int j = 0; j < kEpiGroups - 1; ++j) o[j] = mg[j * 128 + r];
