@@ -105,6 +105,21 @@ void rh_weight_free(rh_weight *w);
 int rh_matmul_quantized_b(rh_ctx *ctx, const rh_weight *w, const float *a, int64_t rows, int64_t k, float *out);
 
 /*
+ * The FP32 head, the engine's default (OcrEngineConfig.quantize_rec_head is false by default,
+ * src/pipeline.rs:59): the MatMul arm then runs matmul_transposed_b (src/ops/matmul.rs:514-897,
+ * dispatched at src/engine/model.rs:1264) on the transposed FP32 weight. rh_weight_pack_f32
+ * keeps no int8: each class row is scaled by an exact power of two and split into fp16 high
+ * and low parts (~22 significant bits, A split likewise), so logits match the FP32 product to
+ * within 1e-4. The returned weight works with rh_matmul_transposed_b (the literal MatMul.12
+ * drop-in in FP32 mode), rh_head_decode[_lines|_device|_ctc] and the device forms;
+ * rh_weight_export/_image and rh_matmul_quantized_b reject it (and rh_matmul_transposed_b
+ * rejects an INT8 weight). Same arguments and errors as rh_weight_pack / rh_matmul_quantized_b.
+ */
+int rh_weight_pack_f32(rh_ctx *ctx, const float *w_nk, int64_t n, int64_t k, const float *bias, int64_t bias_len,
+                       rh_weight **out);
+int rh_matmul_transposed_b(rh_ctx *ctx, const rh_weight *w, const float *a, int64_t rows, int64_t k, float *out);
+
+/*
  * The fused head: for each timestep row r of a [rows][k], the class with the largest
  * probability after softmax over all n classes (first index on ties) and that probability,
  * i.e. matmul_quantized_b -> softmax_inplace (src/ops/softmax.rs:199-285, dispatched by the

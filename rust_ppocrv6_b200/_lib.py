@@ -34,6 +34,7 @@ SIGNATURES = {
     "rh_ctx_num_devices": (_c_int, [_vp]),
     "rh_ctx_set_timeout_ms": (_c_int, [_vp, _c_int]),
     "rh_weight_pack": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _c_i64, ctypes.POINTER(_vp)]),
+    "rh_weight_pack_f32": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _c_i64, ctypes.POINTER(_vp)]),
     "rh_weight_set_bias": (_c_int, [_vp, _vp, _vp, _c_i64]),
     "rh_weight_export": (_c_int, [_vp, _vp, _vp, _vp]),
     "rh_weight_export_image": (_c_int, [_vp, _vp, _vp, _vp]),
@@ -41,6 +42,7 @@ SIGNATURES = {
     "rh_weight_device_bytes": (_c_i64, [_vp]),
     "rh_weight_free": (None, [_vp]),
     "rh_matmul_quantized_b": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _vp]),
+    "rh_matmul_transposed_b": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _vp]),
     "rh_head_decode": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "rh_head_decode_lines": (_c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "rh_head_decode_device": (_c_int, [_vp, _vp, _c_int, _vp, _c_i64, _vp, _vp, _vp]),

@@ -33,7 +33,8 @@ struct HeadParams {
     int hi_steps;              // MMA K-steps of the high fp16 part of A
     int lo_steps;              // MMA K-steps of the low fp16 part of A
     int merged_tail;           // 1: hi step hi_steps-1 also carries lo's last 8 K values
-    const uint8_t* btiles;     // n_chunks * 32 KB, fp16 weight tiles in the smem image order
+    const uint8_t* btiles;     // n_chunks tiles of 32 KB (dual: 64 KB = hi then lo image), smem image order
+    int dual;                  // FP32 weights: each tile holds fp16 hi and lo parts (A_hi.W_lo added)
     const float2* colp;        // n_chunks * 128 (scale, bias); padded columns (0, -inf)
     const float* ctab;         // n_chunks * 256: per tile c[128] = scale*log2(e), e[128] = bias*log2(e)
     int n_mblocks;             // ceil(m / 128)
@@ -57,9 +58,10 @@ struct PackParams {
     int n_pad;                 // n_chunks * 128
     int merged_tail;
     int tail_step;             // index of the last hi K-step (ceil(k/16) - 1)
-    int8_t* q;                 // [n][k] canonical int8 (QuantizedWeight::data)
-    float* scales;             // [n]
-    uint8_t* btiles;           // n_pad/128 tiles of 32 KB
+    int f32;                   // 1: FP32 weights (no int8): per-class power-of-two scale, fp16 hi + lo images
+    int8_t* q;                 // [n][k] canonical int8 (QuantizedWeight::data); unused when f32
+    float* scales;             // [n]; unused when f32
+    uint8_t* btiles;           // n_pad/128 tiles of 32 KB (f32: 64 KB, hi image then lo image)
     float2* colp;              // [n_pad]
     float* ctab;               // [n_pad / 128][256]
 };

@@ -132,6 +132,7 @@ struct rh_ctx {
 
 struct rh_weight {
     int64_t n = 0, k = 0;
+    bool f32 = false;  // FP32 head (rh_weight_pack_f32): hi/lo fp16 images, no int8
     Geometry g{};
     struct Per {
         int device = 0;
@@ -142,7 +143,7 @@ struct rh_weight {
         float* ctab = nullptr;
     };
     std::vector<Per> per;
-    std::vector<float> host_scales;  // QuantizedWeight::scales, kept to rebuild the bias table
+    std::vector<float> host_scales;  // per-class scale (int8 scale, or 2^-sh for FP32), to rebuild the bias table
 };
 
 namespace {
@@ -168,6 +169,7 @@ int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per&
     p.lo_steps = w->g.lo_steps;
     p.merged_tail = w->g.merged;
     p.btiles = pw.tiles;
+    p.dual = w->f32 ? 1 : 0;
     p.colp = pw.colp;
     p.ctab = pw.ctab;
     p.poly_pairs = poly_pairs_setting();
@@ -457,8 +459,9 @@ int rh_ctx_set_timeout_ms(rh_ctx* ctx, int timeout_ms) {
     return RH_OK;
 }
 
-int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len,
-                   rh_weight** out) {
+namespace {
+int pack_weight(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len, bool f32,
+                rh_weight** out) {
     if (int rc = check_ctx(ctx)) return rc;
     if (!out || !w_nk) return fail(RH_ERR_INVALID_ARG, "null weight or output pointer");
     *out = nullptr;
@@ -472,6 +475,7 @@ int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const f
     auto w = std::make_unique<rh_weight>();
     w->n = n;
     w->k = k;
+    w->f32 = f32;
     w->g = geometry(n, k);
     const int n_pad = w->g.n_chunks * rh::kBlockN;
     for (auto& sp : ctx->slots) {
@@ -480,9 +484,11 @@ int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const f
         RH_CUDA(cudaSetDevice(s.device));
         rh_weight::Per p;
         p.device = s.device;
-        RH_CUDA(cudaMalloc(&p.q, (size_t)n * (size_t)k));
-        RH_CUDA(cudaMalloc(&p.scales, (size_t)n * sizeof(float)));
-        RH_CUDA(cudaMalloc(&p.tiles, (size_t)w->g.n_chunks * rh::kTileBytes));
+        if (!f32) {
+            RH_CUDA(cudaMalloc(&p.q, (size_t)n * (size_t)k));
+            RH_CUDA(cudaMalloc(&p.scales, (size_t)n * sizeof(float)));
+        }
+        RH_CUDA(cudaMalloc(&p.tiles, (size_t)w->g.n_chunks * rh::kTileBytes * (f32 ? 2 : 1)));
         RH_CUDA(cudaMalloc(&p.colp, (size_t)n_pad * sizeof(float2)));
         RH_CUDA(cudaMalloc(&p.ctab, (size_t)n_pad * 2 * sizeof(float)));
         w->per.push_back(p);
@@ -504,6 +510,7 @@ int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const f
         pp.n_pad = n_pad;
         pp.merged_tail = w->g.merged;
         pp.tail_step = w->g.tail_step;
+        pp.f32 = f32 ? 1 : 0;
         pp.q = p.q;
         pp.scales = p.scales;
         pp.btiles = p.tiles;
@@ -514,15 +521,28 @@ int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const f
         RH_CUDA(cudaStreamSynchronize(s.stream));
         cudaFree(d_w);
         if (d_b) cudaFree(d_b);
-        if (w->host_scales.empty()) {
-            w->host_scales.resize((size_t)n);
-            RH_CUDA(cudaMemcpyAsync(w->host_scales.data(), p.scales, (size_t)n * sizeof(float),
-                                    cudaMemcpyDeviceToHost, s.stream));
+        if (w->host_scales.empty()) {  // the per-class scale is the .x of the epilogue table
+            std::vector<float2> colp((size_t)n);
+            RH_CUDA(cudaMemcpyAsync(colp.data(), p.colp, (size_t)n * sizeof(float2), cudaMemcpyDeviceToHost,
+                                    s.stream));
             RH_CUDA(cudaStreamSynchronize(s.stream));
+            w->host_scales.resize((size_t)n);
+            for (int64_t j = 0; j < n; ++j) w->host_scales[(size_t)j] = colp[(size_t)j].x;
         }
     }
     *out = w.release();
     return RH_OK;
+}
+}  // namespace
+
+int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len,
+                   rh_weight** out) {
+    return pack_weight(ctx, w_nk, n, k, bias, bias_len, false, out);
+}
+
+int rh_weight_pack_f32(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len,
+                       rh_weight** out) {
+    return pack_weight(ctx, w_nk, n, k, bias, bias_len, true, out);
 }
 
 int rh_weight_set_bias(rh_ctx* ctx, rh_weight* w, const float* bias, int64_t bias_len) {
@@ -540,6 +560,7 @@ int rh_weight_set_bias(rh_ctx* ctx, rh_weight* w, const float* bias, int64_t bia
 int rh_weight_export(rh_ctx* ctx, const rh_weight* w, int8_t* q, float* scales) {
     if (int rc = check_ctx(ctx)) return rc;
     if (!w || w->per.empty()) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (w->f32) return fail(RH_ERR_INVALID_ARG, "an FP32 weight has no int8 data");
     const auto& p = w->per[0];
     RH_CUDA(cudaSetDevice(p.device));
     RH_CUDA(cudaDeviceSynchronize());
@@ -551,6 +572,7 @@ int rh_weight_export(rh_ctx* ctx, const rh_weight* w, int8_t* q, float* scales) 
 int rh_weight_export_image(rh_ctx* ctx, const rh_weight* w, uint8_t* tiles, float* colp) {
     if (int rc = check_ctx(ctx)) return rc;
     if (!w || w->per.empty()) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (w->f32) return fail(RH_ERR_INVALID_ARG, "the image of an FP32 weight is not exported");
     const auto& p = w->per[0];
     RH_CUDA(cudaSetDevice(p.device));
     RH_CUDA(cudaDeviceSynchronize());
@@ -569,6 +591,7 @@ int rh_weight_dims(const rh_weight* w, int64_t* n, int64_t* k) {
 
 int64_t rh_weight_device_bytes(const rh_weight* w) {
     if (!w) return 0;
+    if (w->f32) return (int64_t)w->g.n_chunks * (2 * rh::kTileBytes + rh::kBlockN * 16);
     return w->n * w->k + w->n * 4 + (int64_t)w->g.n_chunks * (rh::kTileBytes + rh::kBlockN * 16);
 }
 
@@ -589,6 +612,20 @@ void rh_weight_free(rh_weight* w) {
 int rh_matmul_quantized_b(rh_ctx* ctx, const rh_weight* w, const float* a, int64_t rows, int64_t k, float* out) {
     if (int rc = check_ctx(ctx)) return rc;
     if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (w->f32) return fail(RH_ERR_INVALID_ARG, "weight was packed FP32: use rh_matmul_transposed_b");
+    if (k != w->k)
+        return fail(RH_ERR_INVALID_ARG,
+                    "Inner dimensions must match: " + std::to_string(k) + " != " + std::to_string(w->k));
+    if (rows < 0) return fail(RH_ERR_INVALID_ARG, "negative row count");
+    if (rows == 0) return RH_OK;
+    if (!a || !out) return fail(RH_ERR_INVALID_ARG, "null input or output");
+    return run_host_on_slot(ctx, w, 0, a, rows, nullptr, nullptr, out);
+}
+
+int rh_matmul_transposed_b(rh_ctx* ctx, const rh_weight* w, const float* a, int64_t rows, int64_t k, float* out) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (!w->f32) return fail(RH_ERR_INVALID_ARG, "weight was packed INT8: use rh_matmul_quantized_b");
     if (k != w->k)
         return fail(RH_ERR_INVALID_ARG,
                     "Inner dimensions must match: " + std::to_string(k) + " != " + std::to_string(w->k));

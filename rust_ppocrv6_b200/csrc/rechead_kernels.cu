@@ -401,6 +401,66 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackParams p) {
     }
 }
 
+// ---------------------------------------------------------------- pack (FP32)
+// The FP32 head (matmul_transposed_b, src/ops/matmul.rs:514-897, used when the engine does not
+// quantise the head): no int8. Each class row is scaled by an exact power of two 2^sh so that
+// max |w| lands in [2^14, 2^15), then split into fp16 hi = fp16(w 2^sh) and
+// lo = fp16(w 2^sh - hi) (~22 significant bits); the tile holds the hi image followed by the lo
+// image, and the class table carries 2^-sh in place of the int8 scale. One warp per class.
+__global__ void __launch_bounds__(256) pack_f32_kernel(const PackParams p) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= p.n_pad) return;
+    const int j = warp;
+    const bool real = j < p.n;
+    float w[4];
+    float max_abs = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int kk = lane + 32 * i;
+        w[i] = (real && kk < p.k) ? p.w[(size_t)j * p.k + kk] : 0.0f;
+        max_abs = fmaxf(max_abs, fabsf(w[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) max_abs = fmaxf(max_abs, __shfl_xor_sync(0xffffffffu, max_abs, o));
+    int sh = 0;
+    if (max_abs > 0.0f && max_abs <= 3.4028235e38f) {
+        const int e = (int)((__float_as_uint(max_abs) >> 23) & 0xFFu) - 127;  // floor(log2) for normals
+        sh = min(max(14 - e, -126), 126);
+    }
+    const float up = __uint_as_float((uint32_t)(127 + sh) << 23);
+    const float down = __uint_as_float((uint32_t)(127 - sh) << 23);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] *= up;  // exact: a power of two
+    const int tile = j >> 7, r = j & 127;
+    if (lane == 0) {
+        const float b = (real && p.bias) ? p.bias[j] : 0.0f;
+        p.colp[j] = real ? make_float2(down, b) : make_float2(0.0f, -CUDART_INF_F);
+        p.ctab[(size_t)tile * 256 + r] = real ? down * kLog2e : 0.0f;
+        p.ctab[(size_t)tile * 256 + 128 + r] = real ? b * kLog2e : -CUDART_INF_F;
+    }
+    uint8_t* img = p.btiles + (size_t)tile * (2 * kTileBytes);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int s = lane * 4 + t;  // K slot 0..127, same slot rule as the int8 image
+        int src = s;
+        if (p.merged_tail && s >= 16 * p.tail_step + 8 && s < 16 * p.tail_step + 16) src = s - 8;
+        const bool ok = real && src < p.k;
+        const int from = src & 31, reg = src >> 5;
+        const float v0 = __shfl_sync(0xffffffffu, w[0], from);
+        const float v1 = __shfl_sync(0xffffffffu, w[1], from);
+        const float v2 = __shfl_sync(0xffffffffu, w[2], from);
+        const float v3 = __shfl_sync(0xffffffffu, w[3], from);
+        const float x = ok ? (reg == 0 ? v0 : reg == 1 ? v1 : reg == 2 ? v2 : v3) : 0.0f;
+        const __half hi = __float2half_rn(x);
+        const __half lo = __float2half_rn(x - __half2float(hi));
+        const uint32_t off = (uint32_t)(s >> 6) * 16384u + (uint32_t)r * 128u +
+                             (uint32_t)((((s & 63) >> 3) ^ (r & 7)) << 4) + (uint32_t)(s & 7) * 2u;
+        *reinterpret_cast<__half*>(img + off) = hi;
+        *reinterpret_cast<__half*>(img + kTileBytes + off) = lo;
+    }
+}
+
 // -------------------------------------------------------------------- head
 // Warp roles (one CTA per SM, persistent over work units = (row block, class range)):
 //   warp 0      lane 0: weight-tile producer (TMA bulk copies into the smem ring)
@@ -469,28 +529,31 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         // The whole warp runs the loop (uniform control flow); one elected lane issues.
+        // FP32 weights: each tile is a 64 KB (hi, lo) pair, so the ring has half as many stages.
+        const uint32_t tile_bytes = p.dual ? 2u * kTileBytes : kTileBytes;
+        const uint32_t nst = p.dual ? kStages / 2 : kStages;
         uint32_t cc = 0, issued = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
             const Unit U = unit_of(u, p);
             for (int c = U.c0; c < U.c1; ++c, ++cc) {
-                const int s = (int)(cc % kStages);
+                const int s = (int)(cc % nst);
                 ok = __all_sync(0xffffffffu,
-                                wait_bar(bar(kBarBEmpty + s), ((cc / kStages) & 1u) ^ 1u, abort_flag, p, 1));
+                                wait_bar(bar(kBarBEmpty + s), ((cc / nst) & 1u) ^ 1u, abort_flag, p, 1));
                 if (!ok) break;
                 if (p.debug_flags & kDebugStallProducer) continue;
                 if (elect_one()) {
-                    mbar_arrive_expect_tx(bar(kBarBFull + s), kTileBytes);
-                    bulk_copy_g2s(base + kOffB + (uint32_t)s * kTileBytes, p.btiles + (size_t)c * kTileBytes,
-                                  kTileBytes, bar(kBarBFull + s));
+                    mbar_arrive_expect_tx(bar(kBarBFull + s), tile_bytes);
+                    bulk_copy_g2s(base + kOffB + (uint32_t)s * tile_bytes, p.btiles + (size_t)c * tile_bytes, tile_bytes,
+                                  bar(kBarBFull + s));
                 }
                 __syncwarp();
                 issued = cc + 1;
             }
         }
         // Drain: the last copy issued into each stage must land before the CTA exits.
-        for (uint32_t s = 0; s < (uint32_t)kStages && s < issued; ++s) {
-            const uint32_t fills = (issued - 1 - s) / kStages + 1;
+        for (uint32_t s = 0; s < nst && s < issued; ++s) {
+            const uint32_t fills = (issued - 1 - s) / nst + 1;
             drain_bar(bar(kBarBFull + (int)s), (fills - 1) & 1u, p);
         }
     } else if (warp == 1) {
@@ -507,6 +570,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             const int kc = step < p.hi_steps ? step : step - p.hi_steps;
             boff[step] = ((uint32_t)(kc >> 2) * 16384u + (uint32_t)(kc & 3) * 32u) >> 4;
         }
+        const uint32_t tile_bytes = p.dual ? 2u * kTileBytes : kTileBytes;
+        const uint32_t nst = p.dual ? kStages / 2 : kStages;
         uint32_t cc = 0, uc = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
@@ -516,16 +581,37 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             tc_fence_after();
             const uint32_t a_tmem = tmem + kTmemA;
             for (int c = U.c0; c < U.c1; ++c, ++cc) {
-                const int s = (int)(cc % kStages);
+                const int s = (int)(cc % nst);
                 const uint32_t buf = cc % kAccBufs;
-                bool w = wait_bar(bar(kBarBFull + s), (cc / kStages) & 1u, abort_flag, p, 3);
+                bool w = wait_bar(bar(kBarBFull + s), (cc / nst) & 1u, abort_flag, p, 3);
                 w = w && wait_bar(bar(kBarAccEmpty + (int)buf), ((cc / kAccBufs) & 1u) ^ 1u, abort_flag, p, 4);
                 ok = __all_sync(0xffffffffu, w);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + kTmemAcc + buf * 128u;
-                const uint64_t bdesc0 = smem_desc_k_sw128(base + kOffB + (uint32_t)s * kTileBytes);
-                if (k120) {
+                const uint64_t bdesc0 = smem_desc_k_sw128(base + kOffB + (uint32_t)s * tile_bytes);
+                if (p.dual) {
+                    if (k120) {
+                        mma_tile_k120_dual_warp(d_tmem, a_tmem, bdesc0, idesc, bar(kBarBEmpty + s),
+                                                bar(kBarAccFull + (int)buf));
+                    } else {
+                        // A_hi.W_hi + A_lo.W_hi, then A_hi.W_lo (lo image 32 KB further)
+#pragma unroll
+                        for (int step = 0; step < 16; ++step) {
+                            if (step < steps)
+                                mma_f16_ts_warp(d_tmem, a_tmem + (uint32_t)step * 8u, bdesc0 + boff[step], idesc,
+                                                step > 0 ? 1u : 0u);
+                        }
+#pragma unroll
+                        for (int step = 0; step < 8; ++step) {
+                            if (step < p.hi_steps)
+                                mma_f16_ts_warp(d_tmem, a_tmem + (uint32_t)step * 8u,
+                                                bdesc0 + (kTileBytes >> 4) + boff[step], idesc, 1u);
+                        }
+                        mma_commit_warp(bar(kBarBEmpty + s));
+                        mma_commit_warp(bar(kBarAccFull + (int)buf));
+                    }
+                } else if (k120) {
                     mma_tile_k120_warp(d_tmem, a_tmem, bdesc0, idesc, bar(kBarBEmpty + s), bar(kBarAccFull + (int)buf));
                 } else if (k80) {
                     mma_tile_k80_warp(d_tmem, a_tmem, bdesc0, idesc, bar(kBarBEmpty + s), bar(kBarAccFull + (int)buf));
@@ -875,7 +961,10 @@ cudaError_t launch_pack(const PackParams& p, cudaStream_t stream) {
     const int threads = 256;
     const long long total = (long long)p.n_pad * 32;
     const int blocks = (int)((total + threads - 1) / threads);
-    pack_kernel<<<blocks, threads, 0, stream>>>(p);
+    if (p.f32)
+        pack_f32_kernel<<<blocks, threads, 0, stream>>>(p);
+    else
+        pack_kernel<<<blocks, threads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -230,6 +230,91 @@ __device__ __forceinline__ void mma_tile_k80_warp(uint32_t d_tmem, uint32_t a_tm
         : "memory");
 }
 
+// FP32 weights, K = 113..120: the 15 MMAs of mma_tile_k120_warp on the hi weight image,
+// then A_hi against the lo weight image (32 KB further in the stage) in 8 more K-steps (the
+// last also adds A_lo(112..119).W_lo, a negligible lo x lo term): 23 MMAs per tile.
+__device__ __forceinline__ void mma_tile_k120_dual_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                        uint32_t bar_b_empty, uint32_t bar_acc_full) {
+    asm volatile(
+        "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 b<23>;\n\t.reg .b32 a<23>;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 pf, 0, 0;\n\t"
+        "setp.eq.b32 pt, 0, 0;\n\t"
+        "add.s64 b0, %2, 0;\n\t"
+        "add.u32 a0, %1, 0;\n\t"
+        "add.s64 b1, %2, 2;\n\t"
+        "add.u32 a1, %1, 8;\n\t"
+        "add.s64 b2, %2, 4;\n\t"
+        "add.u32 a2, %1, 16;\n\t"
+        "add.s64 b3, %2, 6;\n\t"
+        "add.u32 a3, %1, 24;\n\t"
+        "add.s64 b4, %2, 1024;\n\t"
+        "add.u32 a4, %1, 32;\n\t"
+        "add.s64 b5, %2, 1026;\n\t"
+        "add.u32 a5, %1, 40;\n\t"
+        "add.s64 b6, %2, 1028;\n\t"
+        "add.u32 a6, %1, 48;\n\t"
+        "add.s64 b7, %2, 1030;\n\t"
+        "add.u32 a7, %1, 56;\n\t"
+        "add.s64 b8, %2, 0;\n\t"
+        "add.u32 a8, %1, 64;\n\t"
+        "add.s64 b9, %2, 2;\n\t"
+        "add.u32 a9, %1, 72;\n\t"
+        "add.s64 b10, %2, 4;\n\t"
+        "add.u32 a10, %1, 80;\n\t"
+        "add.s64 b11, %2, 6;\n\t"
+        "add.u32 a11, %1, 88;\n\t"
+        "add.s64 b12, %2, 1024;\n\t"
+        "add.u32 a12, %1, 96;\n\t"
+        "add.s64 b13, %2, 1026;\n\t"
+        "add.u32 a13, %1, 104;\n\t"
+        "add.s64 b14, %2, 1028;\n\t"
+        "add.u32 a14, %1, 112;\n\t"
+        "add.s64 b15, %2, 2048;\n\t"
+        "add.u32 a15, %1, 0;\n\t"
+        "add.s64 b16, %2, 2050;\n\t"
+        "add.u32 a16, %1, 8;\n\t"
+        "add.s64 b17, %2, 2052;\n\t"
+        "add.u32 a17, %1, 16;\n\t"
+        "add.s64 b18, %2, 2054;\n\t"
+        "add.u32 a18, %1, 24;\n\t"
+        "add.s64 b19, %2, 3072;\n\t"
+        "add.u32 a19, %1, 32;\n\t"
+        "add.s64 b20, %2, 3074;\n\t"
+        "add.u32 a20, %1, 40;\n\t"
+        "add.s64 b21, %2, 3076;\n\t"
+        "add.u32 a21, %1, 48;\n\t"
+        "add.s64 b22, %2, 3078;\n\t"
+        "add.u32 a22, %1, 56;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], b0, %3, pf;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], b4, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], b5, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], b6, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], b7, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a8], b8, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a9], b9, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a10], b10, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a11], b11, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a12], b12, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a13], b13, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a14], b14, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a15], b15, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a16], b16, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a17], b17, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a18], b18, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a19], b19, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a20], b20, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a21], b21, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a22], b22, %3, pt;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%4];\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(bar_b_empty), "r"(bar_acc_full)
+        : "memory");
+}
+
 // 1 for exactly one lane of the (converged) warp.
 __device__ __forceinline__ bool elect_one() {
     uint32_t e;

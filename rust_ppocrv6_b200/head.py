@@ -174,6 +174,33 @@ class QuantizedWeight:
             pass
 
 
+class Fp32Weight(QuantizedWeight):
+    """The FP32 head weight (the engine's default, quantize_rec_head = false): the transposed
+    [N, K] f32 weight used by matmul_transposed_b (src/ops/matmul.rs:514-897), packed on the
+    GPU as power-of-two-scaled fp16 hi/lo images (rh_weight_pack_f32). No int8 payload."""
+
+    @classmethod
+    def from_f32_transposed(cls, w_t, ctx: Context | None = None, bias=None) -> "Fp32Weight":
+        ctx = ctx or default_context()
+        w_t = _f32(w_t)
+        if w_t.ndim != 2:
+            raise RecHeadError(RH_ERR_INVALID_ARG, f"expected [N, K] weight, got shape {w_t.shape}")
+        n, k = w_t.shape
+        b = None if bias is None else _f32(bias).reshape(-1)
+        h = ctypes.c_void_p()
+        check(load().rh_weight_pack_f32(ctx.handle, _p(w_t), n, k, None if b is None else _p(b),
+                                        0 if b is None else b.size, ctypes.byref(h)))
+        return cls(ctx, h, n, k, b)
+
+    @property
+    def data(self):
+        raise RecHeadError(RH_ERR_INVALID_ARG, "an FP32 weight has no int8 data")
+
+    @property
+    def scales(self):
+        raise RecHeadError(RH_ERR_INVALID_ARG, "an FP32 weight has no int8 scales")
+
+
 def _use_bias(qw: QuantizedWeight, bias) -> None:
     if bias is None:
         if qw.bias is not None:
@@ -206,6 +233,17 @@ def matmul_quantized_b(a, qw: QuantizedWeight, bias=None) -> np.ndarray:
     out = np.empty(lead + (qw.rows,), np.float32)
     if rows:
         check(load().rh_matmul_quantized_b(qw._ctx.handle, qw.handle, _p(a), rows, qw.cols, _p(out)))
+    return out
+
+
+def matmul_transposed_b(a, w: Fp32Weight, bias=None) -> np.ndarray:
+    """The FP32 MatMul.12 drop-in (ops::matmul_transposed_b with an Fp32Weight): logits [..., N]."""
+    a = _f32(a)
+    lead, rows = _rows(a, w.cols)
+    _use_bias(w, bias)
+    out = np.empty(lead + (w.rows,), np.float32)
+    if rows:
+        check(load().rh_matmul_transposed_b(w._ctx.handle, w.handle, _p(a), rows, w.cols, _p(out)))
     return out
 
 

@@ -488,6 +488,82 @@ def test_ctc_decode_from_fused_head(rh, ctx, oracle):
             assert abs(sc - s_ref) <= 1e-5 * max(s_ref, 1e-30)
 
 
+# ------------------------------------------------------------ FP32 head
+
+
+def _oracle_f32_head(oracle, x, w_t, bias):
+    """matmul_transposed_b (exact product) -> softmax_inplace -> find_argmax, per timestep, with
+    the top-2 logit gap for the near-tie rule."""
+    logits = oracle.matmul_f32_transposed_b(x, w_t, bias)
+    probs = oracle.softmax_lastaxis(logits)
+    idx = np.empty(x.shape[0], np.int32)
+    prob = np.empty(x.shape[0], np.float32)
+    for r in range(x.shape[0]):
+        idx[r], prob[r] = oracle.find_argmax(probs[r])
+    top2 = np.sort(logits, axis=1)[:, -2:]
+    return logits, {"idx": idx, "prob": prob, "gap": (top2[:, 1] - top2[:, 0]).astype(np.float32)}
+
+
+@pytest.mark.parametrize("n,k", [(18710, 120), (6906, 80), (1000, 64), (533, 123), (129, 17), (5, 8)])
+def test_fp32_head_logits_match_the_fp32_product(rh, ctx, oracle, n, k):
+    """The engine's default head (quantize_rec_head = false): matmul_transposed_b with FP32
+    weights, against the exact product, for both fast layouts (K=120, K=80) and the generic ones."""
+    rng = np.random.default_rng(41 + n + k)
+    w = (0.05 * rng.standard_normal((n, k))).astype(np.float32)
+    w[0] = 0.0                     # an all-zero class
+    if n > 3:
+        w[1] *= 1e3                # large and tiny rows: the per-class power-of-two scale
+        w[2] *= 1e-20
+    bias = (0.01 * rng.standard_normal(n)).astype(np.float32)
+    fw = rh.Fp32Weight.from_f32_transposed(w, ctx=ctx, bias=bias)
+    x = rng.standard_normal((200, k), dtype=np.float32)
+    got = rh.matmul_transposed_b(x, fw, bias)
+    ref = oracle.matmul_f32_transposed_b(x, w, bias)
+    # any f32 dot product (the reference's FP32 kernel included) is off by up to ~1e-6 of the
+    # sum of |terms|; with cancellation that exceeds 2e-6 of the result, so bound by the terms
+    terms = np.abs(x).astype(np.float64) @ np.abs(w).astype(np.float64).T
+    err = np.abs(got.astype(np.float64) - ref)
+    assert np.all(err <= LOGIT_ABS_TOL + LOGIT_REL_TOL * terms), f"max err {err.max():.3g}"
+    plain = terms < 50.0  # ordinary rows also meet the plain logits bar
+    assert np.all(err[plain] <= LOGIT_ABS_TOL + LOGIT_REL_TOL * np.abs(ref[plain]))
+    fw.free()
+
+
+def test_fp32_head_fused_and_real_weights(rh, ctx, oracle):
+    from rust_ppocrv6_b200 import workloads
+
+    wl = workloads.make(1, scale=6 / 64)
+    fw = rh.Fp32Weight.from_f32_transposed(wl.w_t, ctx=ctx, bias=wl.bias)
+    idx, prob = rh.head_decode(wl.x, fw, line_offsets=wl.line_offsets)
+    _, ref = _oracle_f32_head(oracle, wl.x, wl.w_t, wl.bias)
+    assert_fused(idx, prob, ref, "fp32")
+    # the collapse on the GPU works on the FP32 head too
+    tokens, toff, scores = rh.head_decode_ctc(wl.x, fw, wl.line_offsets)
+    ht, hs = rh.CtcDecoder([]).collapse(idx, prob, wl.line_offsets)
+    np.testing.assert_array_equal(tokens, np.concatenate(ht))
+    fw.free()
+    # a slice of the real head (linear_8.w_0, every 16th class) in FP32
+    import os
+
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "real_head_slice.npz"))
+    fw = rh.Fp32Weight.from_f32_transposed(g["w_t"], ctx=ctx, bias=g["bias"])
+    x = np.random.default_rng(43).standard_normal((300, g["w_t"].shape[1]), dtype=np.float32)
+    assert_logits_close(rh.matmul_transposed_b(x, fw, g["bias"]), oracle.matmul_f32_transposed_b(x, g["w_t"], g["bias"]))
+    idx, prob = rh.head_decode(x, fw)
+    _, ref = _oracle_f32_head(oracle, x, g["w_t"], g["bias"])
+    assert_fused(idx, prob, ref, "fp32-real")
+    # the two weight kinds keep to their own MatMul entry points
+    with pytest.raises(rh.RecHeadError):
+        rh.matmul_quantized_b(x, fw)
+    qw = rh.QuantizedWeight.from_f32_transposed(g["w_t"], ctx=ctx)
+    with pytest.raises(rh.RecHeadError):
+        rh.matmul_transposed_b(x, qw)
+    with pytest.raises(rh.RecHeadError):
+        fw.data
+    qw.free()
+    fw.free()
+
+
 def _collapse_inputs(seed=31):
     """Per-timestep (idx, prob) with blanks and repeats, and line lengths around the warp
     width (0, 1, 31, 32, 33, 64, 65, ...), starting at a non-zero row."""
