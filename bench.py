@@ -43,6 +43,7 @@ def head_dims(workload: str):
     return (workloads.K_TINY, workloads.N_TINY) if workload == "tiny" else (K_DIM, N_CLASSES)
 L2_BYTES = 126 * 1024 * 1024
 METRIC = "W8A32 rec-head decoded timesteps/s (MatMul.12+Add.204 -> Softmax.2 -> argmax)"
+METRIC_F32 = "FP32 rec-head decoded timesteps/s (MatMul.12+Add.204 -> Softmax.2 -> argmax)"
 UNIT = "timesteps/s"
 
 
@@ -53,6 +54,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["cfg2", "cfg3", "tiny"], default="cfg2")
+    ap.add_argument("--weights", choices=["int8", "f32"], default="int8",
+                    help="int8: the quantised head (the metric's path); f32: the engine's default FP32 head")
     ap.add_argument("--cpu-sample-lines", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -203,6 +206,10 @@ def cpu_reference(lines_off: np.ndarray, x: np.ndarray, w_t, bias, sample_lines:
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return
+    if args.weights == "f32":
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU arm times the quantised (int8) head of the "
+                          "metric; the FP32 head has no CPU port here"}), flush=True)
+        return
     off, rows, _, desc, _ = workload_for(args.workload, 1, 0)
     w_t, bias = head_weights(args.workload)
     x = synth(min(rows, int(off[min(args.cpu_sample_lines, off.size - 1)])), 1234, w_t.shape[1])
@@ -268,7 +275,10 @@ def main():
     w_t, bias = head_weights(args.workload)
     k_dim, n_classes = w_t.shape[1], w_t.shape[0]
     ctx = rh.Context(devices=[local])
-    qw = rh.QuantizedWeight.from_f32_transposed(w_t, ctx=ctx, bias=bias)
+    if args.weights == "f32":
+        qw = rh.Fp32Weight.from_f32_transposed(w_t, ctx=ctx, bias=bias)
+    else:
+        qw = rh.QuantizedWeight.from_f32_transposed(w_t, ctx=ctx, bias=bias)
 
     x_host = synth(rows, 1000 + rank, k_dim)
     x_bytes = x_host.nbytes
@@ -343,7 +353,8 @@ def main():
                 "note": "achieved = 2*K*N*rows per step / device time per step (head + merge kernels)"}
 
     out = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": METRIC if args.weights == "int8" else METRIC_F32, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) features, N(0,0.05^2) weights, N(0,0.01^2) bias; no public dataset)",
@@ -355,7 +366,9 @@ def main():
         "roofline": roofline,
         "clocks": clocks.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if args.weights == "f32":
+        out["config"]["weights"] = "f32 (hi/lo fp16 images, 23 MMA K-steps per tile)"
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.weights == "int8":
         v, threads, srows, reps, dt = cpu_reference(off, x_host, w_t, bias, args.cpu_sample_lines)
         out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                                "sample": f"{srows} timesteps ({args.cpu_sample_lines} lines of the workload) "
