@@ -141,6 +141,20 @@ int rh_head_decode(rh_ctx *ctx, const rh_weight *w, const float *a, int64_t rows
 int rh_head_decode_lines(rh_ctx *ctx, const rh_weight *w, const float *a, const int64_t *line_offsets,
                          int64_t n_lines, int64_t k, int32_t *idx, float *prob);
 
+/*
+ * rh_head_decode on the SVTR tail's own layout: x is [batch][k][t_len] (the [B, 120, 1, T]
+ * output after Squeeze.7 and before Transpose.8, src/engine/model.rs:1325-1343, graph nodes
+ * Squeeze.7/Transpose.8), so the transpose to [batch*t_len][k] rows that feeds MatMul.12 is
+ * folded into the kernel's feature loads (each converter thread gathers its timestep row; a
+ * warp reads 32 consecutive timesteps per feature, coalesced). idx/prob are [batch*t_len] in
+ * (b, t) order, exactly what rh_head_decode returns for the transposed rows. Host memory, first
+ * device; the _device form takes device pointers and a stream.
+ */
+int rh_head_decode_kt(rh_ctx *ctx, const rh_weight *w, const float *x, int64_t batch, int64_t k, int64_t t_len,
+                      int32_t *idx, float *prob);
+int rh_head_decode_kt_device(rh_ctx *ctx, const rh_weight *w, int slot, const float *d_x, int64_t batch,
+                             int64_t t_len, int32_t *d_idx, float *d_prob, void *stream);
+
 /* Device-memory forms on context device `slot` (0-based) and `stream` (cudaStream_t, NULL =
  * the legacy default stream). Asynchronous; failures surface at rh_sync(). */
 int rh_head_decode_device(rh_ctx *ctx, const rh_weight *w, int slot, const float *d_a, int64_t rows, int32_t *d_idx,

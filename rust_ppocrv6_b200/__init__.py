@@ -9,12 +9,13 @@ from ._lib import (RH_ERR_CUDA, RH_ERR_DEVICE_FAULT, RH_ERR_INVALID_ARG, RH_ERR_
                    RH_ERR_UNSUPPORTED, RH_OK, RecHeadError, header_symbols, load)
 from .ctc import CtcDecoder
 from .head import (Context, Fp32Weight, QuantizedWeight, ctc_collapse_device, default_context, head_decode,
-                   head_decode_ctc, head_decode_device, matmul_quantized_b, matmul_quantized_b_device,
+                   head_decode_ctc, head_decode_device, head_decode_kt, matmul_quantized_b, matmul_quantized_b_device,
                    matmul_transposed_b)
 
 __all__ = [
-    "Context", "QuantizedWeight", "Fp32Weight", "matmul_transposed_b", "CtcDecoder", "RecHeadError", "matmul_quantized_b", "head_decode",
-    "head_decode_device", "matmul_quantized_b_device", "head_decode_ctc", "ctc_collapse_device",
+    "Context", "QuantizedWeight", "Fp32Weight", "CtcDecoder", "RecHeadError",
+    "matmul_quantized_b", "matmul_transposed_b", "head_decode", "head_decode_kt", "head_decode_ctc",
+    "head_decode_device", "matmul_quantized_b_device", "ctc_collapse_device",
     "default_context", "load", "header_symbols",
     "RH_OK", "RH_ERR_INVALID_ARG", "RH_ERR_CUDA", "RH_ERR_TIMEOUT", "RH_ERR_UNSUPPORTED", "RH_ERR_NO_DEVICE",
     "RH_ERR_DEVICE_FAULT",

@@ -46,6 +46,8 @@ SIGNATURES = {
     "rh_head_decode": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "rh_head_decode_lines": (_c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "rh_head_decode_device": (_c_int, [_vp, _vp, _c_int, _vp, _c_i64, _vp, _vp, _vp]),
+    "rh_head_decode_kt": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp]),
+    "rh_head_decode_kt_device": (_c_int, [_vp, _vp, _c_int, _vp, _c_i64, _c_i64, _vp, _vp, _vp]),
     "rh_matmul_quantized_b_device": (_c_int, [_vp, _vp, _c_int, _vp, _c_i64, _vp, _vp]),
     "rh_head_decode_device_noalloc": (_c_int, [_vp, _vp, _c_int, _vp, _c_i64, _vp, _vp, _vp]),
     "rh_sync": (_c_int, [_vp, _c_int]),

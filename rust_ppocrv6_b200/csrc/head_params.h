@@ -25,7 +25,9 @@ constexpr int kDebugStallProducer = 1;
 constexpr int kDefaultPolyPairs = 0;
 
 struct HeadParams {
-    const float* a;            // [m][k] timestep features (rows packed densely)
+    const float* a;            // [m][k] timestep features (rows packed densely), or [b][k][t_len] (a_t > 0)
+    long long a_t;             // 0: row-major rows; T > 0: a is the SVTR tail's [batch][k][T] (before
+                               // Transpose.8), row r = (r / T, r % T) and element k sits T floats apart
     long long m;
     int k;
     int n;

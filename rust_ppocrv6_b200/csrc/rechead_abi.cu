@@ -155,12 +155,14 @@ int check_ctx(rh_ctx* ctx) {
 
 // Enqueues the head (and the split merge) for rows [0, rows) of d_a on `stream`.
 int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per& pw, const float* d_a, int64_t rows,
-                 int32_t* d_idx, float* d_prob, float* d_logits, bool emit_logits, cudaStream_t stream) {
+                 int32_t* d_idx, float* d_prob, float* d_logits, bool emit_logits, cudaStream_t stream,
+                 int64_t a_t = 0) {
     if (rows <= 0) return RH_OK;
     int n_mblocks, n_splits, cps, grid;
     plan(rows, w->g.n_chunks, s.sms, n_mblocks, n_splits, cps, grid);
     rh::HeadParams p{};
     p.a = d_a;
+    p.a_t = a_t;
     p.m = rows;
     p.k = (int)w->k;
     p.n = (int)w->n;
@@ -711,6 +713,53 @@ int rh_head_decode_lines(rh_ctx* ctx, const rh_weight* w, const float* a, const 
         if (rc[d] != RH_OK) return fail(rc[d], msg[d]);
     }
     return RH_OK;
+}
+
+int rh_head_decode_kt_device(rh_ctx* ctx, const rh_weight* w, int slot, const float* d_x, int64_t batch,
+                             int64_t t_len, int32_t* d_idx, float* d_prob, void* stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (slot < 0 || slot >= (int)ctx->slots.size()) return fail(RH_ERR_INVALID_ARG, "slot out of range");
+    if (batch < 0 || t_len < 0) return fail(RH_ERR_INVALID_ARG, "negative batch or sequence length");
+    if (batch == 0 || t_len == 0) return RH_OK;
+    if (!d_x || !d_idx || !d_prob) return fail(RH_ERR_INVALID_ARG, "null device pointer");
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this device");
+    return enqueue_head(ctx, w, s, *pw, d_x, batch * t_len, d_idx, d_prob, nullptr, false, (cudaStream_t)stream,
+                        t_len);
+}
+
+int rh_head_decode_kt(rh_ctx* ctx, const rh_weight* w, const float* x, int64_t batch, int64_t k, int64_t t_len,
+                      int32_t* idx, float* prob) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (k != w->k)
+        return fail(RH_ERR_INVALID_ARG,
+                    "Inner dimensions must match: " + std::to_string(k) + " != " + std::to_string(w->k));
+    if (batch < 0 || t_len < 0) return fail(RH_ERR_INVALID_ARG, "negative batch or sequence length");
+    const int64_t rows = batch * t_len;
+    if (rows == 0) return RH_OK;
+    if (!x || !idx || !prob) return fail(RH_ERR_INVALID_ARG, "null input or output");
+    Slot& s = *ctx->slots[0];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
+    const size_t x_bytes = (size_t)rows * (size_t)k * sizeof(float);
+    RH_CUDA(s.a.ensure(x_bytes));
+    RH_CUDA(s.idx.ensure((size_t)rows * sizeof(int32_t)));
+    RH_CUDA(s.prob.ensure((size_t)rows * sizeof(float)));
+    RH_CUDA(cudaMemcpyAsync(s.a.p, x, x_bytes, cudaMemcpyHostToDevice, s.stream));
+    if (int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, (int32_t*)s.idx.p, (float*)s.prob.p, nullptr,
+                              false, s.stream, t_len))
+        return rc;
+    RH_CUDA(cudaMemcpyAsync(idx, s.idx.p, (size_t)rows * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaMemcpyAsync(prob, s.prob.p, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    return read_status(s);
 }
 
 int rh_head_decode_device(rh_ctx* ctx, const rh_weight* w, int slot, const float* d_a, int64_t rows, int32_t* d_idx,

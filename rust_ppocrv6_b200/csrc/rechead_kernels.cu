@@ -127,8 +127,8 @@ __device__ __noinline__ void drain_bar(uint32_t bar, uint32_t parity, const Head
 // part, steps [hi_steps, hi_steps + lo_steps) the low part; with a merged tail the last
 // high step holds hi(16T..16T+7) in slots 0..7 and lo(16T..16T+7) in slots 8..15 (the
 // weight tile repeats q[16T..16T+7] in the matching K slots).
-__device__ __forceinline__ __half a_part(const float* arow, bool valid, int k, float rs, int step, int j,
-                                         int hi_steps, int merged) {
+__device__ __forceinline__ __half a_part(const float* arow, long long stride, bool valid, int k, float rs, int step,
+                                         int j, int hi_steps, int merged) {
     int kk;
     bool want_lo;
     if (step < hi_steps) {
@@ -144,7 +144,7 @@ __device__ __forceinline__ __half a_part(const float* arow, bool valid, int k, f
         want_lo = true;
     }
     if (!valid || kk >= k) return __float2half_rn(0.0f);
-    const float x = __ldg(arow + kk) * rs;
+    const float x = __ldg(arow + (long long)kk * stride) * rs;
     const __half h = __float2half_rn(x);
     if (!want_lo) return h;
     return __float2half_rn(x - __half2float(h));
@@ -668,8 +668,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         // are bulk-copied into shared memory while the current unit runs, so the A switch at a
         // unit boundary is a shared-memory -> TMEM conversion.
         const bool merged120 = p.hi_steps == 8 && p.lo_steps == 7 && p.merged_tail;
+        const bool kt = p.a_t > 0;  // [batch][k][T] input: gathered by the converters themselves
         const bool staged = (merged120 || (!p.merged_tail && p.lo_steps == p.hi_steps)) && (p.k % 4) == 0 &&
-                            ((reinterpret_cast<uintptr_t>(p.a) & 15u) == 0);
+                            (kt || (reinterpret_cast<uintptr_t>(p.a) & 15u) == 0);
+        const bool bulk = staged && !kt;  // row-major: one bulk copy per unit
         const uint32_t lo_col = 8u * (uint32_t)p.hi_steps;  // first TMEM column of the low part
         const float* stage_g = reinterpret_cast<const float*>(gbase + kOffAStage);
         auto issue_stage = [&](int u) {  // one thread: rows of unit u -> staging buffer
@@ -680,19 +682,34 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             mbar_arrive_expect_tx(bar(kBarStageFull), bytes);
             bulk_copy_g2s(base + kOffAStage, p.a + r0 * p.k, bytes, bar(kBarStageFull));
         };
+        // [batch][k][T]: thread r gathers row r of unit u into the staging buffer (for one k the
+        // 32 lanes of a warp read 32 consecutive timesteps: coalesced), while the previous unit runs.
+        float* my_stage = const_cast<float*>(stage_g) + (size_t)r * p.k;
+        auto gather_row = [&](int u) {
+            const Unit V = unit_of(u, p);
+            const long long row = (long long)V.mb * kBlockM + r;
+            if (row >= p.m) return;
+            const float* src = p.a + (row / p.a_t) * (long long)p.k * p.a_t + row % p.a_t;
+            for (int kk = 0; kk < p.k; ++kk) my_stage[kk] = __ldg(src + (long long)kk * p.a_t);
+        };
         uint32_t staged_issued = 0, staged_used = 0;
-        if (staged && r == 0 && (int)blockIdx.x < units) {
+        if (bulk && r == 0 && (int)blockIdx.x < units) {
             issue_stage(blockIdx.x);
             staged_issued = 1;
         }
+        if (staged && kt && (int)blockIdx.x < units) gather_row(blockIdx.x);
+        const long long astride = kt ? p.a_t : 1;
         uint32_t uc = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc) {
             const Unit U = unit_of(u, p);
             const uint32_t slot = uc & 3u;
             const long long row = (long long)U.mb * kBlockM + r;
             const bool valid = row < p.m;
-            const float* arow = staged ? stage_g + (size_t)r * p.k : p.a + (valid ? row : 0) * (long long)p.k;
-            if (staged) {
+            const long long vrow = valid ? row : 0;
+            const float* arow = staged ? stage_g + (size_t)r * p.k
+                                : kt ? p.a + (vrow / p.a_t) * (long long)p.k * p.a_t + vrow % p.a_t
+                                     : p.a + vrow * (long long)p.k;
+            if (bulk) {
                 if (!__all_sync(0xffffffffu, wait_bar(bar(kBarStageFull), uc & 1u, abort_flag, p, 12))) break;
                 staged_used = uc + 1;
             }
@@ -704,7 +721,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                         max_abs = fmaxf(max_abs, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
                     }
                 } else {
-                    for (int kk = 0; kk < p.k; ++kk) max_abs = fmaxf(max_abs, fabsf(__ldg(arow + kk)));
+                    for (int kk = 0; kk < p.k; ++kk) max_abs = fmaxf(max_abs, fabsf(__ldg(arow + (long long)kk * astride)));
                 }
             }
             // fp16 holds the parts only below 65504: rows with max|a| >= 2^14 are scaled by a
@@ -754,7 +771,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                         tmem_st32x32b_x4(a_t + 60u, l4);
                     }
                 }
-                mbar_arrive(bar(kBarStageRead));
+                if (bulk) mbar_arrive(bar(kBarStageRead));
             } else {
                 for (int g4 = 0; g4 * 4 < steps; ++g4) {
                     uint32_t wv[32];
@@ -766,9 +783,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                             uint32_t packed = 0u;
                             if (step < steps) {
                                 const __half lo_h =
-                                    a_part(arow, valid, p.k, rs, step, 2 * w, p.hi_steps, p.merged_tail);
+                                    a_part(arow, astride, valid, p.k, rs, step, 2 * w, p.hi_steps, p.merged_tail);
                                 const __half hi_h =
-                                    a_part(arow, valid, p.k, rs, step, 2 * w + 1, p.hi_steps, p.merged_tail);
+                                    a_part(arow, astride, valid, p.k, rs, step, 2 * w + 1, p.hi_steps, p.merged_tail);
                                 packed = (uint32_t)__half_as_ushort(lo_h) | ((uint32_t)__half_as_ushort(hi_h) << 16);
                             }
                             wv[t * 8 + w] = packed;
@@ -784,8 +801,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             mbar_arrive(bar(kBarAFull));
             mbar_arrive(bar(kBarRhoFull + (int)slot));
             // next unit's rows into the staging buffer once every converter has read this one
+            if (staged && kt && u + (int)gridDim.x < units) gather_row(u + (int)gridDim.x);
             bool stop = false;
-            if (staged && r == 0 && u + (int)gridDim.x < units) {
+            if (bulk && r == 0 && u + (int)gridDim.x < units) {
                 if (wait_bar(bar(kBarStageRead), uc & 1u, abort_flag, p, 13)) {
                     issue_stage(u + (int)gridDim.x);
                     ++staged_issued;
@@ -796,7 +814,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             if (__any_sync(0xffffffffu, stop)) break;  // leave the loop as a whole warp
         }
         // a staged copy still in flight must land before the CTA exits
-        if (staged && r == 0 && staged_issued > staged_used) drain_bar(bar(kBarStageFull), (staged_issued - 1) & 1u, p);
+        if (bulk && r == 0 && staged_issued > staged_used) drain_bar(bar(kBarStageFull), (staged_issued - 1) & 1u, p);
     } else if (warp >= 8) {
         // ------------------------------------------------------------- epilogue
         // Each quarter is one 32-column TMEM load; the accumulator goes back to the MMA

@@ -271,6 +271,22 @@ def head_decode(a, qw: QuantizedWeight, bias=None, line_offsets=None):
     return idx.reshape(lead), prob.reshape(lead)
 
 
+def head_decode_kt(x, qw: QuantizedWeight, bias=None):
+    """head_decode on the SVTR tail's [batch, k, T] output (before Transpose.8), the transpose
+    folded into the kernel: returns (idx int32 [batch, T], prob f32 [batch, T])."""
+    x = _f32(x)
+    if x.ndim != 3 or x.shape[1] != qw.cols:
+        raise RecHeadError(RH_ERR_INVALID_ARG, f"expected [batch, {qw.cols}, T] features, got {x.shape}")
+    if bias is not None:
+        _use_bias(qw, bias)
+    b, k, t = x.shape
+    idx = np.empty((b, t), np.int32)
+    prob = np.empty((b, t), np.float32)
+    if b * t:
+        check(load().rh_head_decode_kt(qw._ctx.handle, qw.handle, _p(x), b, k, t, _p(idx), _p(prob)))
+    return idx, prob
+
+
 def head_decode_ctc(a, qw: QuantizedWeight, line_offsets, bias=None):
     """The head of a line batch with the CTC collapse on the GPU (rh_head_decode_ctc):
     returns (tokens int32 [total], token_offsets int64 [n_lines + 1], scores f32 [n_lines]),

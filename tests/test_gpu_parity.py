@@ -564,6 +564,35 @@ def test_fp32_head_fused_and_real_weights(rh, ctx, oracle):
     fw.free()
 
 
+@pytest.mark.parametrize("n,k,batch,t,f32", [(18710, 120, 50, 37, False), (6906, 80, 9, 200, False),
+                                              (700, 123, 7, 33, False), (18710, 120, 6, 129, True)])
+def test_head_on_svtr_layout_equals_transposed_rows(rh, ctx, oracle, n, k, batch, t, f32):
+    """rh_head_decode_kt takes the SVTR tail's [batch, k, T] output (Transpose.8 folded into the
+    kernel's loads); it must return exactly what rh_head_decode returns for the transposed rows,
+    through the staged path (K % 4 == 0), the generic strided path (K = 123) and the FP32 head."""
+    rng = np.random.default_rng(51 + k + t)
+    w = (0.05 * rng.standard_normal((n, k))).astype(np.float32)
+    bias = (0.01 * rng.standard_normal(n)).astype(np.float32)
+    x = rng.standard_normal((batch, k, t), dtype=np.float32)
+    x[1, :, 3] *= 3e4  # a row on the power-of-two rescaled path
+    kind = rh.Fp32Weight if f32 else rh.QuantizedWeight
+    qw = kind.from_f32_transposed(w, ctx=ctx, bias=bias)
+    idx_kt, prob_kt = rh.head_decode_kt(x, qw)
+    rows = np.ascontiguousarray(x.transpose(0, 2, 1).reshape(-1, k))
+    idx, prob = rh.head_decode(rows, qw)
+    np.testing.assert_array_equal(idx_kt.reshape(-1), idx)
+    np.testing.assert_array_equal(prob_kt.reshape(-1), prob)
+    if not f32 and k == 120:
+        q, s = oracle.pack(w)
+        off = np.arange(0, batch * t + 1, t, dtype=np.int64)
+        ref = oracle.head_decode(rows, off, q, s, bias, threads=8, want_gap=True)
+        plain = np.ones(rows.shape[0], bool)
+        plain[1 * t + 3] = False
+        mism = idx != ref["idx"]
+        assert np.all(ref["gap"][mism & plain] < TIE_GAP)
+    qw.free()
+
+
 def _collapse_inputs(seed=31):
     """Per-timestep (idx, prob) with blanks and repeats, and line lengths around the warp
     width (0, 1, 31, 32, 33, 64, 65, ...), starting at a non-zero row."""
