@@ -1,0 +1,53 @@
+"""The benchmark's CPU-side contract: the reference arm (`bench.py --impl reference`, which
+the round-end driver runs beside ours) prints one JSON line with the fields it promises, and
+the helpers the GPU arm uses (workload shapes, sharding, the committed traffic figure)
+behave. Nothing here needs a GPU."""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _run(*args):
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], capture_output=True, text=True,
+                         timeout=300, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out.stdout
+    return json.loads(lines[0])
+
+
+def test_reference_arm_prints_the_contract_line():
+    rec = _run("--impl", "reference", "--steps", "1", "--warmup", "0", "--cpu-sample-lines", "4")
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in rec, key
+    assert rec["impl"] == "reference" and rec["unit"] == "timesteps/s" and rec["value"] > 0
+    assert rec["e2e"]["h2d_bytes_per_step"] == 0 and rec["e2e"]["d2h_bytes_per_step"] == 0
+    assert rec["cpu_baseline"]["kind"] == "port" and rec["cpu_baseline"]["cores"] >= 1
+    assert "workload" in rec["config"]
+
+
+def test_reference_arm_for_the_fp32_head_reports_unavailable():
+    rec = _run("--impl", "reference", "--weights", "f32", "--steps", "1", "--warmup", "0")
+    assert rec["impl"] == "reference" and "unavailable" in rec
+
+
+def test_bench_helpers():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    off, rows, global_rows, desc, scaling = bench.workload_for("cfg2", 4, 1)
+    assert rows == 122880 and global_rows == 4 * 122880 and scaling == "weak"
+    off, rows, global_rows, desc, scaling = bench.workload_for("cfg3", 2, 0)
+    assert scaling == "strong" and 0 < rows < global_rows and off[0] == 0 and off[-1] == rows
+    assert bench.head_dims("tiny") == (80, 6906) and bench.head_dims("cfg2") == (120, 18710)
+    w, b = bench.head_weights("tiny")
+    assert w.shape == (6906, 80) and b.shape == (6906,)
+    t = bench.profiled_traffic()
+    assert t is None or t > 60_000_000  # DRAM bytes of one cfg2 launch from the committed ncu summary
+    assert np.all(np.diff(off) >= 0)
