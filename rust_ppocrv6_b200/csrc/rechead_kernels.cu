@@ -5,7 +5,9 @@
 //                GPU: per-class symmetric int8 + f32 scale, bit-exact; also writes the
 //                tensor-core image of the weight (fp16 tiles in shared-memory order) and the
 //                per-class epilogue tables.
-//  head_kernel   persistent, warp-specialised W8A32 projection. A (f32 features) is split
+//  pack_f32_kernel  the FP32 head's weight (matmul_transposed_b, src/ops/matmul.rs:514-897):
+//                per-class power-of-two scale, fp16 hi and lo images, epilogue tables.
+//  head_kernel   persistent, warp-specialised W8A32 (or FP32) projection. A (f32 features) is split
 //                into two fp16 parts in TMEM, weight tiles stream in through TMA bulk copies,
 //                tcgen05.mma accumulates in TMEM, and the epilogue applies scale + bias and
 //                either
