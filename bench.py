@@ -103,14 +103,21 @@ def head_weights(workload: str = "cfg2"):
 
 
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+    """Samples the SM clock and throttle reasons through NVML from a background thread that is
+    started before the warm-up (so NVML is warm and sampling is steady when timing begins);
+    `window(t0, t1)` keeps the samples taken inside the timed region (host perf_counter)."""
+
+    NAMES = {
+        "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
 
     def __init__(self, device_index: int):
-        self.samples = []
-        self.reasons = set()
+        self.samples = []  # (perf_counter, sm MHz, throttle-reason bits)
         self.max_mhz = None
         self._stop = threading.Event()
         self._ok = False
+        self._t0 = self._t1 = None
         try:
             import pynvml
 
@@ -124,40 +131,36 @@ class ClockSampler:
 
     def _run(self):
         nv = self._nv
-        names = {
-            "hw_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwSlowdown", 0x8),
-            "hw_thermal_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwThermalSlowdown", 0x40),
-            "sw_thermal_slowdown": getattr(nv, "nvmlClocksThrottleReasonSwThermalSlowdown", 0x20),
-            "sw_power_cap": getattr(nv, "nvmlClocksThrottleReasonSwPowerCap", 0x4),
-            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwPowerBrakeSlowdown", 0x80),
-        }
         while not self._stop.is_set():
             try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
-                r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
-                for k, bit in names.items():
-                    if r & bit:
-                        self.reasons.add(k)
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.samples.append((time.perf_counter(), mhz, bits))
             except Exception:
                 pass
-            time.sleep(0.002)
+            time.sleep(0.001)
 
-    def __enter__(self):
+    def start(self):
         if self._ok:
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
 
-    def __exit__(self, *exc):
+    def stop(self):
         if self._ok:
             self._stop.set()
             self._t.join()
 
+    def window(self, t0: float, t1: float):
+        self._t0, self._t1 = t0, t1
+
     def summary(self):
         if not self._ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
-        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
-                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        inside = [x for x in self.samples if self._t0 is None or self._t0 <= x[0] <= self._t1]
+        reasons = sorted({k for _, _, bits in inside for k, bit in self.NAMES.items() if bits & bit})
+        return {"sm_mhz": statistics.median([m for _, m, _ in inside]) if inside else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside)}
 
 
 def measured_peak_tflops():
@@ -295,6 +298,7 @@ def main():
     def step(i):
         rh.head_decode_device(qw, xs[i % n_copies].data_ptr(), rows, idx.data_ptr(), prob.data_ptr(), sptr)
 
+    clocks = ClockSampler(local).start()
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
@@ -304,12 +308,14 @@ def main():
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        ev0.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i)
-        ev1.record(stream)
-        torch.cuda.synchronize()
+    t_start = time.perf_counter()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks.window(t_start, time.perf_counter())
+    clocks.stop()
     barrier()
     ctx.sync()
     launches = ctx.launch_count(0) - l0
