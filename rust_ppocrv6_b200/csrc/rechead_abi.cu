@@ -35,6 +35,10 @@ int fail(int code, const std::string& msg) {
 struct DevBuf {
     void* p = nullptr;
     size_t cap = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    ~DevBuf() { release(); }  // the owner has made the right device current
     cudaError_t ensure(size_t bytes) {
         if (bytes <= cap && p) return cudaSuccess;
         if (p) cudaFree(p);
@@ -62,6 +66,17 @@ struct Slot {
     DevBuf lines, tok_off, tokens, scores;  // CTC collapse on the device
     std::mutex mu;
     int64_t launches = 0;
+    // Frees everything, also on a context whose creation failed part-way.
+    ~Slot() {
+        cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        if (copy_stream) cudaStreamSynchronize(copy_stream);
+        for (DevBuf* b : {&a, &idx, &prob, &out, &partial, &lines, &tok_off, &tokens, &scores}) b->release();
+        if (d_status) cudaFree(d_status);
+        if (copied) cudaEventDestroy(copied);
+        if (copy_stream) cudaStreamDestroy(copy_stream);
+        if (stream) cudaStreamDestroy(stream);
+    }
 };
 
 struct Geometry {
@@ -144,6 +159,18 @@ struct rh_weight {
     };
     std::vector<Per> per;
     std::vector<float> host_scales;  // per-class scale (int8 scale, or 2^-sh for FP32), to rebuild the bias table
+    // Frees every device copy, also for a weight whose packing failed part-way.
+    ~rh_weight() {
+        for (auto& p : per) {
+            cudaSetDevice(p.device);
+            cudaDeviceSynchronize();
+            cudaFree(p.q);
+            cudaFree(p.scales);
+            cudaFree(p.tiles);
+            cudaFree(p.colp);
+            cudaFree(p.ctab);
+        }
+    }
 };
 
 namespace {
@@ -434,22 +461,7 @@ int rh_ctx_create(const int* devices, int n_devices, rh_ctx** out) {
 }
 
 void rh_ctx_destroy(rh_ctx* ctx) {
-    if (!ctx) return;
-    for (auto& s : ctx->slots) {
-        cudaSetDevice(s->device);
-        cudaStreamSynchronize(s->stream);
-        s->a.release();
-        s->idx.release();
-        s->prob.release();
-        s->out.release();
-        s->partial.release();
-        if (s->d_status) cudaFree(s->d_status);
-        if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
-        if (s->copied) cudaEventDestroy(s->copied);
-        if (s->copy_stream) cudaStreamDestroy(s->copy_stream);
-        if (s->stream) cudaStreamDestroy(s->stream);
-    }
-    delete ctx;
+    delete ctx;  // each Slot waits for its streams and frees its buffers
 }
 
 int rh_ctx_num_devices(const rh_ctx* ctx) { return ctx ? (int)ctx->slots.size() : 0; }
@@ -494,14 +506,16 @@ int pack_weight(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const floa
         RH_CUDA(cudaMalloc(&p.colp, (size_t)n_pad * sizeof(float2)));
         RH_CUDA(cudaMalloc(&p.ctab, (size_t)n_pad * 2 * sizeof(float)));
         w->per.push_back(p);
-        float* d_w = nullptr;
+        DevBuf tw, tb;  // temporaries, freed on every path
+        RH_CUDA(tw.ensure((size_t)n * (size_t)k * sizeof(float)));
+        float* d_w = static_cast<float*>(tw.p);
         float* d_b = nullptr;
-        RH_CUDA(cudaMalloc(&d_w, (size_t)n * (size_t)k * sizeof(float)));
         // Stream-ordered copies: a plain cudaMemcpy from pageable memory may return before its
         // DMA lands, and the pack kernel runs on a non-blocking stream.
         RH_CUDA(cudaMemcpyAsync(d_w, w_nk, (size_t)n * (size_t)k * sizeof(float), cudaMemcpyHostToDevice, s.stream));
         if (bias) {
-            RH_CUDA(cudaMalloc(&d_b, (size_t)n * sizeof(float)));
+            RH_CUDA(tb.ensure((size_t)n * sizeof(float)));
+            d_b = static_cast<float*>(tb.p);
             RH_CUDA(cudaMemcpyAsync(d_b, bias, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, s.stream));
         }
         rh::PackParams pp{};
@@ -521,8 +535,6 @@ int pack_weight(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const floa
         RH_CUDA(rh::launch_pack(pp, s.stream));
         s.launches++;
         RH_CUDA(cudaStreamSynchronize(s.stream));
-        cudaFree(d_w);
-        if (d_b) cudaFree(d_b);
         if (w->host_scales.empty()) {  // the per-class scale is the .x of the epilogue table
             std::vector<float2> colp((size_t)n);
             RH_CUDA(cudaMemcpyAsync(colp.data(), p.colp, (size_t)n * sizeof(float2), cudaMemcpyDeviceToHost,
@@ -598,17 +610,7 @@ int64_t rh_weight_device_bytes(const rh_weight* w) {
 }
 
 void rh_weight_free(rh_weight* w) {
-    if (!w) return;
-    for (auto& p : w->per) {
-        cudaSetDevice(p.device);
-        cudaDeviceSynchronize();
-        cudaFree(p.q);
-        cudaFree(p.scales);
-        cudaFree(p.tiles);
-        cudaFree(p.colp);
-        cudaFree(p.ctab);
-    }
-    delete w;
+    delete w;  // frees every device copy
 }
 
 int rh_matmul_quantized_b(rh_ctx* ctx, const rh_weight* w, const float* a, int64_t rows, int64_t k, float* out) {

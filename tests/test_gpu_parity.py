@@ -391,6 +391,49 @@ def test_fused_rows_are_independent_of_batch(rh, ctx):
         assert np.max(np.abs(prob - prob_all[lo:hi]) / prob_all[lo:hi]) < 2e-6
 
 
+def test_full_size_cfg3_properties_and_sampled_parity(rh, ctx, oracle):
+    """BASELINE's cfg3 at full size (8192 ragged lines, ~530k timesteps): many waves, class
+    splits and the pipelined host path. Size-independent checks on every row (the host path,
+    the device path and the GPU collapse agree; idx in range; prob in (0, 1] and >= 1/N),
+    plus the oracle on a random sample of 256 rows."""
+    import torch
+
+    from rust_ppocrv6_b200 import workloads
+
+    rng = np.random.default_rng(workloads.SEED + 3)
+    off = workloads.ragged_offsets(rng, 8192)
+    m = int(off[-1])
+    assert m > 400_000
+    w, b = workloads.head_weights(np.random.default_rng(workloads.SEED + 7))
+    x = np.random.default_rng(61).standard_normal((m, workloads.K), dtype=np.float32)
+    qw = rh.QuantizedWeight.from_f32_transposed(w, ctx=ctx, bias=b)
+    idx, prob = rh.head_decode(x, qw, line_offsets=off)
+    assert idx.min() >= 0 and idx.max() < workloads.N
+    assert np.all(prob <= 1.0 + 1e-6) and np.all(prob >= (1.0 - 1e-5) / workloads.N)
+    # device-resident path over the same rows: identical (same plan for the same row count)
+    dx = torch.from_numpy(x).cuda()
+    di = torch.empty(m, dtype=torch.int32, device="cuda")
+    dp = torch.empty(m, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    rh.head_decode_device(qw, dx.data_ptr(), m, di.data_ptr(), dp.data_ptr())
+    ctx.sync()
+    np.testing.assert_array_equal(di.cpu().numpy(), idx)
+    np.testing.assert_allclose(dp.cpu().numpy(), prob, rtol=2e-6)
+    # the GPU collapse of the whole batch equals the host collapse of the host path's output
+    tokens, toff, scores = rh.head_decode_ctc(x, qw, off)
+    ht, hs = rh.CtcDecoder([]).collapse(idx, prob, off)
+    np.testing.assert_array_equal(toff, np.concatenate([[0], np.cumsum([t.size for t in ht])]))
+    np.testing.assert_array_equal(tokens, np.concatenate(ht))
+    np.testing.assert_allclose(scores, hs, rtol=2e-6)
+    # oracle on a random sample of rows
+    sample = np.sort(np.random.default_rng(62).choice(m, size=256, replace=False))
+    q, s = oracle.pack(w)
+    xs = np.ascontiguousarray(x[sample])
+    ref = oracle.head_decode(xs, np.arange(0, 257, dtype=np.int64), q, s, b, threads=8, want_gap=True)
+    assert_fused(idx[sample], prob[sample], ref, "cfg3-sample")
+    qw.free()
+
+
 # ----------------------------------------------------------- boundary / errors
 
 
