@@ -434,6 +434,40 @@ def test_full_size_cfg3_properties_and_sampled_parity(rh, ctx, oracle):
     qw.free()
 
 
+def test_concurrent_calls_from_worker_threads(rh, ctx):
+    """The engine calls the head from up to rec_batch_threads Rayon workers at once
+    (src/pipeline.rs:417-427); calls on one context are serialised per device inside the
+    library, so concurrent callers get exactly the sequential results."""
+    import threading
+
+    from rust_ppocrv6_b200 import workloads
+
+    wl = workloads.make(1, scale=0.25)
+    qw = rh.QuantizedWeight.from_f32_transposed(wl.w_t, ctx=ctx, bias=wl.bias)
+    rng = np.random.default_rng(71)
+    inputs = [rng.standard_normal((int(rng.integers(1, 900)), workloads.K), dtype=np.float32) for _ in range(12)]
+    expect = [rh.head_decode(x, qw) for x in inputs]
+    got = [None] * len(inputs)
+    errors = []
+
+    def work(i):
+        try:
+            for _ in range(3):
+                got[i] = rh.head_decode(inputs[i], qw)
+        except Exception as e:  # surfaced below
+            errors.append(e)
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(len(inputs))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for (ei, ep), (gi, gp) in zip(expect, got):
+        assert np.array_equal(ei, gi) and np.array_equal(ep, gp)
+    qw.free()
+
+
 # ----------------------------------------------------------- boundary / errors
 
 
