@@ -216,6 +216,16 @@ constexpr float kAbsLo = -60.0f, kAbsHi = 100.0f;
 // a word with another tag counts as no threshold). The threshold never exceeds the unit's
 // true maximum, so the quarter that holds the first maximum is always searched, while the
 // other groups stop searching quarters that cannot win.
+// First index i in [B, B+8) with t[i] == q (the caller knows one exists).
+template <int B>
+__device__ __forceinline__ int first_in_octant(const float* t, float q) {
+    int f = B + 7;
+#pragma unroll
+    for (int i = B + 6; i >= B; --i)
+        if (t[i] == q) f = i;
+    return f;
+}
+
 template <bool SCALED, int NPOLY, bool FIRST>
 __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, uint32_t es, int col0,
                                               float rho, uint32_t rowmax, uint32_t tag, RowState& st) {
@@ -237,12 +247,14 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
         t[i + 2] = t23.x;
         t[i + 3] = t23.y;
     }
-    float r1[11];
+    // max over the quarter through the maxima of its four 8-column octants (kept for the
+    // first-argmax search, which then scans one octant instead of 32 columns)
+    float oct[4];
 #pragma unroll
-    for (int i = 0; i < 10; ++i) r1[i] = max3f(t[3 * i], t[3 * i + 1], t[3 * i + 2]);
-    r1[10] = fmaxf(t[30], t[31]);
-    const float qmax = max3f(max3f(r1[0], r1[1], r1[2]), max3f(r1[3], r1[4], r1[5]),
-                             max3f(max3f(r1[6], r1[7], r1[8]), r1[9], r1[10]));
+    for (int j = 0; j < 4; ++j)
+        oct[j] = max3f(max3f(t[8 * j], t[8 * j + 1], t[8 * j + 2]), max3f(t[8 * j + 3], t[8 * j + 4], t[8 * j + 5]),
+                       fmaxf(t[8 * j + 6], t[8 * j + 7]));
+    const float qmax = max3f(oct[0], oct[1], fmaxf(oct[2], oct[3]));
     if constexpr (FIRST) {  // first columns of this row in the unit: pick the mode
         // (no early return for padded-only columns: every lane reaches the warp votes below)
         st.off = qmax == -CUDART_INF_F ? -CUDART_INF_F : (qmax >= kAbsLo && qmax <= kAbsHi) ? 0.0f : qmax;
@@ -301,10 +313,16 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
         st.thr = thr ? ord_f32(thr) : -CUDART_INF_F;
         const uint32_t qo = f32_ord(qmax);
         if (qo >= thr) {
-            int first = 31;
-#pragma unroll
-            for (int i = 31; i >= 0; --i)
-                if (t[i] == qmax) first = i;
+            // first octant holding the maximum, then the first column of it within that octant
+            int first;
+            if (oct[0] == qmax)
+                first = first_in_octant<0>(t, qmax);
+            else if (oct[1] == qmax)
+                first = first_in_octant<8>(t, qmax);
+            else if (oct[2] == qmax)
+                first = first_in_octant<16>(t, qmax);
+            else
+                first = first_in_octant<24>(t, qmax);
             st.best = qmax;
             st.idx = col0 + first;
             if (qo > thr) atom_max_shared_u64(rowmax, ((unsigned long long)tag << 32) | qo);
