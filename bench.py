@@ -1,6 +1,7 @@
 """Benchmark: decoded timesteps/s of the fused W8A32 recognition head on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg3]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2|cfg3|tiny|recpre]
 
 One step = one pass of the hot path (MatMul.12 + Add.204 -> Softmax.2 -> per-timestep
 argmax) over one batch. Default workload cfg2: 1024 text lines x T=120 timesteps per GPU
@@ -16,6 +17,9 @@ instead shards one global 8192-line ragged batch over the ranks (strong scaling)
 --impl reference  times the reference algorithm's CPU implementation (the C restatement in
          oracle/, all host threads, lines spread over workers like src/pipeline.rs:417-427)
          on bounded samples of the same workload.
+--workload recpre  the producer side instead: batched recognition preprocessing
+         (RecPreprocess::process of 1024 text-line crops per GPU, each resized to 48 x 960,
+         packed into [1024, 3, 48, 960]) in lines/s, HBM roofline.
 """
 from __future__ import annotations
 
@@ -45,6 +49,9 @@ L2_BYTES = 126 * 1024 * 1024
 METRIC = "W8A32 rec-head decoded timesteps/s (MatMul.12+Add.204 -> Softmax.2 -> argmax)"
 METRIC_F32 = "FP32 rec-head decoded timesteps/s (MatMul.12+Add.204 -> Softmax.2 -> argmax)"
 UNIT = "timesteps/s"
+RECPRE_METRIC = ("rec preprocessing lines/s (RecPreprocess::process: triangle resize to 48 rows + normalise, "
+                 "packed [N,3,48,Wmax])")
+RECPRE_UNIT = "lines/s"
 
 
 def parse():
@@ -53,7 +60,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "tiny"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "tiny", "recpre"], default="cfg2")
     ap.add_argument("--weights", choices=["int8", "f32"], default="int8",
                     help="int8: the quantised head (the metric's path); f32: the engine's default FP32 head")
     ap.add_argument("--cpu-sample-lines", type=int, default=512)
@@ -172,6 +179,15 @@ def measured_peak_tflops():
         return 1590.0, "fallback 1.59 PFLOP/s bf16 dense"
 
 
+def measured_hbm_gbs():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured HBM copy (MEASURED_PEAKS.json)"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s"
+
+
 def profiled_traffic():
     """DRAM bytes (read + write) of one cfg2 head-kernel launch, from the committed ncu summary."""
     import re
@@ -206,8 +222,64 @@ def cpu_reference(lines_off: np.ndarray, x: np.ndarray, w_t, bias, sample_lines:
     return rows * reps / dt, threads, rows, reps, dt
 
 
+def recpre_workload(rank: int, n_lines: int = 1024):
+    """Seeded text-line crops: heights U{24..64}, width 20 x height (every line resizes to
+    48 x 960, the input of one cfg2 line), random bytes. Returns (blob, offsets, widths, heights)."""
+    from rust_ppocrv6_b200 import workloads
+
+    rng = np.random.default_rng(workloads.SEED + 5 + rank)
+    heights = rng.integers(24, 65, n_lines).astype(np.uint32)
+    widths = (20 * heights).astype(np.uint32)
+    sizes = widths.astype(np.int64) * heights * 3
+    offsets = np.zeros(n_lines, np.int64)
+    offsets[1:] = np.cumsum(sizes)[:-1]
+    blob = rng.integers(0, 256, int(sizes.sum()), dtype=np.uint8)
+    return blob, offsets, widths, heights
+
+
+RECPRE_DESC = ("recpre: 1024 RGB8 text-line crops per GPU, h~U{24..64}, w=20h (mean 44 x 880), each resized "
+               "to 48 x 960 and packed into [1024,3,48,960] f32")
+
+
+def cpu_recpre(blob, offsets, widths, heights, sample_lines: int, target_s: float = 10.0, steps: int | None = None,
+               warmup: int = 1):
+    """Times the oracle's preprocessing (RecPreprocess::process + build_batch restated) on the
+    first `sample_lines` crops with every host thread. Returns (lines/s, threads, lines, reps, s)."""
+    from oracle import oracle
+
+    n = min(sample_lines, len(widths))
+    crops = [blob[offsets[i]:offsets[i] + int(widths[i]) * int(heights[i]) * 3].reshape(int(heights[i]),
+                                                                                            int(widths[i]), 3)
+             for i in range(n)]
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    t0 = time.perf_counter()
+    for _ in range(max(warmup, 1)):
+        oracle.rec_preprocess_batch(crops, threads=threads)
+    one = (time.perf_counter() - t0) / max(warmup, 1)
+    reps = steps if steps is not None else max(1, int(np.ceil(target_s / max(one, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.rec_preprocess_batch(crops, threads=threads)
+    dt = time.perf_counter() - t0
+    return n * reps / dt, threads, n, reps, dt
+
+
 def run_reference_arm(args, world, rank):
     if rank != 0:
+        return
+    if args.workload == "recpre":
+        blob, offsets, widths, heights = recpre_workload(0)
+        v, threads, n, reps, dt = cpu_recpre(blob, offsets, widths, heights, min(args.cpu_sample_lines, 256),
+                                             steps=args.steps, warmup=args.warmup)
+        sample = f"{n} crops of the workload per step"
+        print(json.dumps({
+            "impl": "reference", "metric": RECPRE_METRIC, "value": v, "unit": RECPRE_UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / reps, "higher_is_better": True,
+            "scaling": "none (host CPU)", "vs_baseline": None, "dtype": "u8->f32",
+            "data": "synthetic (seeded random RGB8 crops)", "config": {"workload": RECPRE_DESC, "sample": sample},
+            "cpu_baseline": {"value": v, "unit": RECPRE_UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": RECPRE_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
         return
     if args.weights == "f32":
         print(json.dumps({"impl": "reference", "unavailable": "the CPU arm times the quantised (int8) head of the "
@@ -242,6 +314,105 @@ def run_reference_arm(args, world, rank):
     }), flush=True)
 
 
+def run_recpre(args, world, rank, local, torch, rh, barrier, max_over_ranks):
+    """Batched recognition preprocessing: device-resident throughput (rh_rec_preprocess_device,
+    crops already in HBM), end to end through rh_rec_preprocess (pinned host crops in, pinned
+    host tensor out), HBM roofline of the step, CPU baseline."""
+    import ctypes
+
+    blob, offsets, widths, heights = recpre_workload(rank)
+    n = len(widths)
+    out_w, out_h, wmax = rh.batch_shape(widths, heights)
+    out_len = n * 3 * out_h * wmax
+    ctx = rh.Context(devices=[local])
+    d_blobs = [torch.from_numpy(blob).cuda()]
+    d_blobs.append(d_blobs[0].roll(1).contiguous())  # two copies: 2 x 119 MB > L2
+    d_out = torch.empty(out_len, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+
+    def step(i):
+        rh.rec_preprocess_device(ctx, d_blobs[i % 2].data_ptr(), blob.size, offsets, widths, heights,
+                                 d_out.data_ptr(), out_len, stream=sptr)
+
+    clocks = ClockSampler(local).start()
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    ctx.sync()
+    l0 = ctx.launch_count(0)
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    t_start = time.perf_counter()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks.window(t_start, time.perf_counter())
+    clocks.stop()
+    barrier()
+    ctx.sync()
+    launches = ctx.launch_count(0) - l0
+    dev_ms = ev0.elapsed_time(ev1)
+    dev_ms_max = max_over_ranks(dev_ms)
+    value = n * world * args.steps / (dev_ms_max / 1e3)
+
+    # end to end through the host API
+    lib = rh.load()
+    pin_in = torch.from_numpy(blob).pin_memory()
+    pin_out = torch.empty(out_len, dtype=torch.float32).pin_memory()
+    got_w = np.zeros(n, np.uint32)
+    got_max = ctypes.c_uint32(0)
+    vp = ctypes.c_void_p
+
+    def e2e_step():
+        rh._lib.check(lib.rh_rec_preprocess(ctx.handle, vp(pin_in.data_ptr()), blob.size,
+                                            offsets.ctypes.data_as(vp), widths.ctypes.data_as(vp),
+                                            heights.ctypes.data_as(vp), n, 48, 960, vp(pin_out.data_ptr()), out_len,
+                                            got_w.ctypes.data_as(vp), ctypes.byref(got_max)))
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+
+    # roofline: algorithmic bytes = every crop byte read once + every output float written once
+    alg_bytes = int(blob.size) + out_len * 4
+    achieved = alg_bytes / (dev_ms / args.steps / 1e3) / 1e9
+    peak, peak_src = measured_hbm_gbs()
+    out = {
+        "metric": RECPRE_METRIC, "value": value, "unit": RECPRE_UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8->f32",
+        "data": "synthetic (seeded random RGB8 crops; no public dataset)",
+        "config": {"workload": RECPRE_DESC, "lines_per_step": n * world, "parallelism": f"crops sharded x{world}",
+                   "l2": f"crops rotate over 2 device copies ({2 * blob.size / 2**20:.0f} MiB), output "
+                         f"{out_len * 4 / 2**20:.0f} MiB per step (> L2)"},
+        "e2e": {"value": n * world * args.steps / e2e_s, "unit": RECPRE_UNIT, "h2d_bytes_per_step": int(blob.size),
+                "d2h_bytes_per_step": int(out_len * 4), "ms_per_step": e2e_s * 1e3 / args.steps},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_src, "traffic": None,
+                     "note": "achieved = (crop bytes + output bytes) per step / device time per step (tap-table "
+                             "kernel + resize kernel + descriptor copy)"},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, ns, reps, dt = cpu_recpre(blob, offsets, widths, heights, min(args.cpu_sample_lines, 256))
+        out["cpu_baseline"] = {"value": v, "unit": RECPRE_UNIT, "cores": threads, "kind": "port",
+                               "sample": f"{ns} crops of the workload x {reps} passes, {dt:.1f} s wall"}
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
     world, rank, local = dist_env()
@@ -273,6 +444,12 @@ def main():
         t = torch.tensor([v], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.workload == "recpre":
+        run_recpre(args, world, rank, local, torch, rh, barrier, max_over_ranks)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     off, rows, global_rows, desc, scaling = workload_for(args.workload, world, rank)
     w_t, bias = head_weights(args.workload)

@@ -234,6 +234,51 @@ int rh_ctc_collapse_device(rh_ctx *ctx, int slot, const int32_t *d_idx, const fl
 int rh_head_decode_ctc(rh_ctx *ctx, const rh_weight *w, const float *a, const int64_t *line_offsets, int64_t n_lines,
                        int64_t k, int32_t *tokens, int64_t *token_offsets, float *scores);
 
+/* ------------------------------------------------ batched recognition preprocessing
+ *
+ * The producer side of the head: text-line crops (RGB8, row-major HWC, 3 bytes per pixel)
+ * into the recognition network's input tensor. Per crop this is RecPreprocess::process
+ * (src/preprocess/rec.rs:60-105): width = clamp(ceil(H * w / max(h, 1)), 32, max(max_w, 32))
+ * with H = max(target_h, 1); resize_exact(width, H, FilterType::Triangle) of the `image`
+ * crate (0.25); v / 127.5 - 1 into channel planes. The batch is packed as the reference's
+ * batching proof of concept packs it (tools/profiling/batch_poc.rs:14-32): out
+ * [n_lines][3][H][wmax] f32, wmax = the largest width in the batch, columns past a line's
+ * width = +1.0 (white). An empty crop (w or h == 0) resizes to black (-1.0).
+ */
+
+/* RecPreprocess::process's output width for one crop (src/preprocess/rec.rs:62-75).
+ * Host only: needs no context or GPU. */
+uint32_t rh_rec_resized_width(uint32_t orig_w, uint32_t orig_h, uint32_t target_h, uint32_t max_w);
+
+/* Shape of a batch (host only): out_widths[n_lines] (may be NULL), H and wmax. Lets a caller
+ * size the output of rh_rec_preprocess. RH_ERR_UNSUPPORTED for target_h > 2^20 or a crop
+ * side > 2^30. */
+int rh_rec_batch_shape(const uint32_t *widths, const uint32_t *heights, int64_t n_lines, uint32_t target_h,
+                       uint32_t max_w, uint32_t *out_widths, uint32_t *out_h, uint32_t *out_wmax);
+
+/*
+ * Batched preprocessing from host memory, sharded over the context's devices (equal line
+ * counts). Crop l is widths[l] x heights[l] pixels at byte rgb_offsets[l] of rgb[0, rgb_len).
+ * out: host, >= n_lines * 3 * H * wmax floats (out_len); out_widths (may be NULL) and
+ * *out_wmax (may be NULL) receive the batch shape. Replaces the per-crop loop
+ * `self.rec_preprocess.process(&cropped_patch)` of OcrEngine::recognize
+ * (src/pipeline.rs:379) plus build_batch. RH_ERR_INVALID_ARG: a crop outside the pixel
+ * buffer, a short output; RH_ERR_UNSUPPORTED: a crop that shrinks by more than 8190x
+ * horizontally (its filter window would not fit the kernel's shared-memory stage), sizes above
+ * the limits of rh_rec_batch_shape.
+ */
+int rh_rec_preprocess(rh_ctx *ctx, const uint8_t *rgb, int64_t rgb_len, const int64_t *rgb_offsets,
+                      const uint32_t *widths, const uint32_t *heights, int64_t n_lines, uint32_t target_h,
+                      uint32_t max_w, float *out, int64_t out_len, uint32_t *out_widths, uint32_t *out_wmax);
+
+/* As rh_rec_preprocess with the crops (d_rgb) and the output (d_out) in device memory of
+ * `slot`'s device, enqueued on `stream` (0 = the legacy default stream); offsets and sizes
+ * stay in host memory. Asynchronous: device-side errors surface at rh_sync. */
+int rh_rec_preprocess_device(rh_ctx *ctx, int slot, const uint8_t *d_rgb, int64_t rgb_len, const int64_t *rgb_offsets,
+                             const uint32_t *widths, const uint32_t *heights, int64_t n_lines, uint32_t target_h,
+                             uint32_t max_w, float *d_out, int64_t out_len, uint32_t *out_widths, uint32_t *out_wmax,
+                             void *stream);
+
 #ifdef __cplusplus
 }
 #endif

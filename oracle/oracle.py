@@ -38,8 +38,8 @@ def lib() -> ctypes.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    src = os.path.join(_HERE, "ref_w8a32.c")
-    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, f) for f in ("ref_w8a32.c", "ref_rec_pre.c", "Makefile")]
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
         build()
     L = ctypes.CDLL(_LIB_PATH)
     L.oracle_cpu_has_avx2_fma.restype = _int
@@ -60,6 +60,18 @@ def lib() -> ctypes.CDLL:
     L.oracle_matmul_f32_transposed_b.argtypes = [_f32p, _i64, _i64, _f32p, _i64, _vp, _f32p]
     L.oracle_exp_poly.argtypes = [ctypes.c_float]
     L.oracle_exp_poly.restype = ctypes.c_float
+    _u32 = ctypes.c_uint32
+    _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+    _u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+    L.oracle_rec_resized_width.argtypes = [_u32, _u32, _u32, _u32]
+    L.oracle_rec_resized_width.restype = _u32
+    L.oracle_resize_triangle_rgb8.argtypes = [_u8p, _u32, _u32, _u32, _u32, _u8p]
+    L.oracle_resize_triangle_rgb8.restype = _int
+    L.oracle_rec_preprocess.argtypes = [_u8p, _u32, _u32, _u32, _u32, _f32p, ctypes.POINTER(_u32)]
+    L.oracle_rec_preprocess.restype = _int
+    L.oracle_rec_preprocess_batch.argtypes = [_u8p, _i64p, _u32p, _u32p, _i64, _u32, _u32, _f32p, _u32p,
+                                              ctypes.POINTER(_u32), _int]
+    L.oracle_rec_preprocess_batch.restype = _int
     _lib = L
     return L
 
@@ -218,3 +230,63 @@ def matmul_f32_transposed_b(a, b_t, bias=None):
 
 def exp_poly(x: float) -> float:
     return float(lib().oracle_exp_poly(float(x)))
+
+
+# ------------------------------------------------------------ rec preprocessing
+
+def rec_resized_width(w: int, h: int, target_h: int = 48, max_w: int = 960) -> int:
+    """RecPreprocess::process's width rule (src/preprocess/rec.rs:62-75)."""
+    return int(lib().oracle_rec_resized_width(w, h, target_h, max_w))
+
+
+def resize_triangle_rgb8(img: np.ndarray, new_w: int, new_h: int) -> np.ndarray:
+    """image 0.25 resize_exact(new_w, new_h, FilterType::Triangle) of an RGB8 [h,w,3] array."""
+    img = _c(img, np.uint8)
+    h, w = img.shape[:2]
+    out = np.zeros((new_h, new_w, 3), np.uint8)
+    if img.size == 0:
+        img = np.zeros(1, np.uint8)
+    rc = lib().oracle_resize_triangle_rgb8(img.reshape(-1), w, h, new_w, new_h, out.reshape(-1))
+    if rc:
+        raise RuntimeError("oracle resize failed")
+    return out
+
+
+def rec_preprocess(img: np.ndarray, target_h: int = 48, max_w: int = 960) -> np.ndarray:
+    """RecPreprocess::process (src/preprocess/rec.rs:60-105): RGB8 [h,w,3] -> f32 [1,3,H,W]."""
+    img = _c(img, np.uint8)
+    h, w = img.shape[:2]
+    th = max(target_h, 1)
+    tw = rec_resized_width(w, h, target_h, max_w)
+    out = np.empty((1, 3, th, tw), np.float32)
+    got = ctypes.c_uint32(0)
+    flat = img.reshape(-1) if img.size else np.zeros(1, np.uint8)
+    rc = lib().oracle_rec_preprocess(flat, w, h, target_h, max_w, out.reshape(-1), ctypes.byref(got))
+    if rc:
+        raise RuntimeError("oracle rec_preprocess failed")
+    return out
+
+
+def rec_preprocess_batch(crops, target_h: int = 48, max_w: int = 960, threads: int = 1):
+    """Batched RecPreprocess::process + build_batch (tools/profiling/batch_poc.rs:14-32):
+    list of RGB8 [h_i,w_i,3] arrays -> (f32 [N,3,H,Wmax] padded with +1.0, widths u32 [N])."""
+    widths = np.array([c.shape[1] for c in crops], np.uint32)
+    heights = np.array([c.shape[0] for c in crops], np.uint32)
+    sizes = np.array([c.size for c in crops], np.int64)
+    offsets = np.zeros(len(crops), np.int64)
+    if len(crops):
+        offsets[1:] = np.cumsum(sizes)[:-1]
+    blob = np.concatenate([_c(c, np.uint8).reshape(-1) for c in crops]) if len(crops) else np.zeros(0, np.uint8)
+    if blob.size == 0:
+        blob = np.zeros(1, np.uint8)
+    th = max(target_h, 1)
+    wmax = max([rec_resized_width(int(w), int(h), target_h, max_w) for w, h in zip(widths, heights)], default=0)
+    out = np.empty((len(crops), 3, th, wmax), np.float32)
+    out_w = np.zeros(len(crops), np.uint32)
+    got = ctypes.c_uint32(0)
+    flat = out.reshape(-1) if out.size else np.zeros(1, np.float32)
+    rc = lib().oracle_rec_preprocess_batch(blob, offsets, widths, heights, len(crops), target_h, max_w, flat, out_w,
+                                           ctypes.byref(got), threads)
+    if rc:
+        raise RuntimeError("oracle rec_preprocess_batch failed")
+    return out, out_w

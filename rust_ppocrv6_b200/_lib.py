@@ -23,6 +23,7 @@ RH_ERR_DEVICE_FAULT = 6
 
 _c_int, _c_i64, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p
 _i64p = ctypes.POINTER(ctypes.c_int64)
+_u32 = ctypes.c_uint32
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -55,6 +56,11 @@ SIGNATURES = {
     "rh_ctc_collapse": (_c_i64, [_vp, _vp, _vp, _c_i64, _vp, _vp, _vp]),
     "rh_ctc_collapse_device": (_c_int, [_vp, _c_int, _vp, _vp, _vp, _c_i64, _vp, _vp, _vp, _vp]),
     "rh_head_decode_ctc": (_c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _vp, _vp, _vp]),
+    "rh_rec_resized_width": (_u32, [_u32, _u32, _u32, _u32]),
+    "rh_rec_batch_shape": (_c_int, [_vp, _vp, _c_i64, _u32, _u32, _vp, _vp, _vp]),
+    "rh_rec_preprocess": (_c_int, [_vp, _vp, _c_i64, _vp, _vp, _vp, _c_i64, _u32, _u32, _vp, _c_i64, _vp, _vp]),
+    "rh_rec_preprocess_device": (_c_int, [_vp, _c_int, _vp, _c_i64, _vp, _vp, _vp, _c_i64, _u32, _u32, _vp, _c_i64,
+                                          _vp, _vp, _vp]),
 }
 
 _lib = None

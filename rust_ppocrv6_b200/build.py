@@ -16,7 +16,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "librechead.so")
-SOURCES = ["rechead_kernels.cu", "ctc_kernels.cu", "rechead_abi.cu"]
+SOURCES = ["rechead_kernels.cu", "ctc_kernels.cu", "recpre_kernels.cu", "rechead_abi.cu"]
 HEADERS = ["head_params.h", "sm100_ptx.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

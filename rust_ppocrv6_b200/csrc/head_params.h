@@ -16,6 +16,9 @@ constexpr int kHeadThreads = 32 * (8 + 4 * kEpiGroups);  // 32 warps, see head_k
 
 // Device status word bits (status[0]); status[1] records which wait gave up.
 constexpr int kDevTimeout = 1;
+// Recognition preprocessing: a tap window or a staged column span exceeded the size the host
+// planned for it (the access was skipped; never expected).
+constexpr int kDevRecPlan = 2;
 // Test-only: the weight producer never fills its stages, so every consumer's bounded wait
 // runs out and the kernel must return kDevTimeout with the context intact.
 constexpr int kDebugStallProducer = 1;
@@ -68,6 +71,37 @@ struct PackParams {
     float* ctab;               // [n_pad / 128][256]
 };
 
+// Batched recognition preprocessing (recpre_kernels.cu): RecPreprocess::process of each crop
+// (resize to out_h rows with the triangle filter, normalise to [-1, 1]) packed into one
+// [n_lines][3][out_h][wmax] tensor whose columns past a line's width are +1.0 (white).
+constexpr int kRecThreads = 256;   // threads per block; also the most output columns per staged chunk
+constexpr int kRecSpanMax = 16384; // most staged input columns (3 x 16384 f32 = 192 KB of shared memory)
+
+struct RecLine {
+    long long src;     // byte offset of the crop (RGB8, row-major HWC) in the pixel buffer
+    int w, h;          // crop size in pixels; a zero means an empty crop (resized to black)
+    int out_w;         // resized width
+    int stride_x;      // weight slots per output column (>= its tap count)
+    int stride_y;      // weight slots per output row
+    int chunk;         // output columns staged at once (1..kRecThreads)
+    long long coord;   // first (first tap, tap count) entry: out_w column entries, then out_h row entries
+    long long wts;     // first weight: out_w * stride_x column weights, then out_h * stride_y row weights
+};
+
+struct RecParams {
+    const uint8_t* rgb;  // crops
+    const RecLine* lines;
+    long long n_lines;
+    int out_h;           // rows per line (target height, at least 1)
+    int wmax;            // columns per line in the output (the largest resized width)
+    int span_cap;        // staged columns (shared memory: 3 x span_cap f32)
+    int2* coords;        // tap windows
+    float* wts;          // normalised tap weights
+    float* out;          // [n_lines][3][out_h][wmax]
+    float inv;           // 1 / 127.5 in f32
+    int* status;         // [2]
+};
+
 // Kernel launchers (rechead_kernels.cu).
 cudaError_t launch_pack(const PackParams& p, cudaStream_t stream);
 cudaError_t launch_head(const HeadParams& p, bool emit_logits, int grid, cudaStream_t stream);
@@ -76,6 +110,9 @@ cudaError_t launch_merge(const float4* partial, int n_splits, long long m, int32
 // CTC greedy collapse of per-timestep (idx, prob) in device memory (ctc_kernels.cu).
 cudaError_t launch_ctc_collapse(const int32_t* idx, const float* prob, const int64_t* line_offsets, int64_t n_lines,
                                 int32_t* tokens, int64_t* token_offsets, float* scores, cudaStream_t stream);
+// Tap windows and weights of every line (one launch), then the resize of lines [line0, line0 + n).
+cudaError_t launch_rec_weights(const RecParams& p, cudaStream_t stream);
+cudaError_t launch_rec_resize(const RecParams& p, long long line0, long long n, cudaStream_t stream);
 size_t head_smem_bytes();
 cudaError_t head_kernel_setup();
 

@@ -4,6 +4,7 @@
 // runs the sm_100a kernels of rechead_kernels.cu or fails.
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -64,6 +65,7 @@ struct Slot {
     int* d_status = nullptr;
     DevBuf a, idx, prob, out, partial;
     DevBuf lines, tok_off, tokens, scores;  // CTC collapse on the device
+    DevBuf pre_rgb, pre_lines, pre_coords, pre_wts, pre_out;  // recognition preprocessing
     std::mutex mu;
     int64_t launches = 0;
     // Frees everything, also on a context whose creation failed part-way.
@@ -71,7 +73,9 @@ struct Slot {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
         if (copy_stream) cudaStreamSynchronize(copy_stream);
-        for (DevBuf* b : {&a, &idx, &prob, &out, &partial, &lines, &tok_off, &tokens, &scores}) b->release();
+        for (DevBuf* b : {&a, &idx, &prob, &out, &partial, &lines, &tok_off, &tokens, &scores, &pre_rgb, &pre_lines,
+                          &pre_coords, &pre_wts, &pre_out})
+            b->release();
         if (d_status) cudaFree(d_status);
         if (copied) cudaEventDestroy(copied);
         if (copy_stream) cudaStreamDestroy(copy_stream);
@@ -401,6 +405,186 @@ int noalloc_scratch(int device, float4** out) {
     }
     *out = static_cast<float4*>(g_noalloc_ptr[device]);
     return RH_OK;
+}
+
+// ------------------------------------------------------ recognition preprocessing
+// Target staged span when choosing a line's chunk (24 KB of shared memory per block); lines
+// that downscale so much that even one output column needs more than rh::kRecSpanMax input
+// columns are rejected as unsupported.
+constexpr double kRecSpanTarget = 2048.0;
+constexpr uint32_t kRecMaxDim = 1u << 30;   // crop sides above this are rejected
+constexpr uint32_t kRecMaxHeight = 1u << 20;  // target heights above this are rejected
+
+// `v as u32` for f32 (saturating, NaN -> 0).
+uint32_t f32_as_u32(float v) {
+    if (!(v > 0.0f)) return 0;
+    if (v >= 4294967296.0f) return UINT32_MAX;
+    return (uint32_t)v;
+}
+
+// RecPreprocess::process's width rule (src/preprocess/rec.rs:62-75).
+uint32_t rec_width(uint32_t w, uint32_t h, uint32_t target_h, uint32_t max_w) {
+    const uint32_t hh = std::max<uint32_t>(h, 1), th = std::max<uint32_t>(target_h, 1);
+    const uint32_t mw = std::max<uint32_t>(max_w, 32);
+    const float aspect = (float)w / (float)hh;
+    return std::min(std::max(f32_as_u32(std::ceil((float)th * aspect)), 32u), mw);
+}
+
+// Upper bound of the input columns that `chunk` consecutive output columns of a w -> out_w
+// axis read: (chunk - 1) * ratio + 2 s + 2, plus 2 for f32 rounding of the window ends.
+long long rec_span_bound(double ratio, double s, int chunk) {
+    return (long long)std::ceil((chunk - 1) * ratio + 2.0 * s + 4.0);
+}
+
+struct RecBatch {
+    std::vector<uint32_t> out_w;
+    uint32_t out_h = 1, wmax = 0;
+};
+
+// Validates a batch (dimensions, crop byte ranges inside [0, rgb_len)) and computes its shape.
+int rec_validate(const int64_t* offs, const uint32_t* widths, const uint32_t* heights, int64_t n, uint32_t target_h,
+                 uint32_t max_w, int64_t rgb_len, RecBatch& b) {
+    if (n < 0) return fail(RH_ERR_INVALID_ARG, "negative line count");
+    if (n > 0 && (!widths || !heights)) return fail(RH_ERR_INVALID_ARG, "null crop sizes");
+    b.out_h = std::max<uint32_t>(target_h, 1);
+    if (b.out_h > kRecMaxHeight) return fail(RH_ERR_UNSUPPORTED, "target height above 2^20");
+    b.out_w.resize((size_t)n);
+    b.wmax = 0;
+    for (int64_t l = 0; l < n; ++l) {
+        const uint32_t w = widths[l], h = heights[l];
+        if (w > kRecMaxDim || h > kRecMaxDim)
+            return fail(RH_ERR_UNSUPPORTED, "crop " + std::to_string(l) + " has a side above 2^30 pixels");
+        b.out_w[l] = rec_width(w, h, target_h, max_w);
+        b.wmax = std::max(b.wmax, b.out_w[l]);
+        if (w == 0 || h == 0) continue;
+        if (offs) {
+            const int64_t bytes = (int64_t)w * (int64_t)h * 3;
+            if (offs[l] < 0 || offs[l] > rgb_len || bytes > rgb_len - offs[l])
+                return fail(RH_ERR_INVALID_ARG, "crop " + std::to_string(l) + " (" + std::to_string(w) + " x " +
+                                                    std::to_string(h) + " RGB8 at byte " + std::to_string(offs[l]) +
+                                                    ") lies outside the pixel buffer of " + std::to_string(rgb_len) +
+                                                    " bytes");
+        }
+        const double rx = (double)w / (double)b.out_w[l];
+        if (rec_span_bound(rx, std::max(rx, 1.0), 1) > rh::kRecSpanMax)
+            return fail(RH_ERR_UNSUPPORTED, "crop " + std::to_string(l) + " (" + std::to_string(w) + " x " +
+                                                std::to_string(h) + ") shrinks by more than " +
+                                                std::to_string(rh::kRecSpanMax / 2 - 2) +
+                                                "x horizontally; split it or pre-scale it");
+    }
+    return RH_OK;
+}
+
+// Line descriptors of lines [l0, l1) of a validated batch, crop bytes rebased by `base`;
+// tables are laid out from 0. span_cap receives the largest staged span the lines need.
+void rec_describe(const int64_t* offs, const uint32_t* widths, const uint32_t* heights, int64_t l0, int64_t l1,
+                  const RecBatch& b, int64_t base, std::vector<rh::RecLine>& lines, long long& n_coords,
+                  long long& n_wts, int& span_cap) {
+    lines.resize((size_t)(l1 - l0));
+    n_coords = 0;
+    n_wts = 0;
+    span_cap = 1;
+    for (int64_t l = l0; l < l1; ++l) {
+        rh::RecLine& L = lines[l - l0];
+        L = rh::RecLine{};
+        L.w = (int)widths[l];
+        L.h = (int)heights[l];
+        L.out_w = (int)b.out_w[l];
+        L.chunk = 1;
+        if (L.w == 0 || L.h == 0) {
+            L.w = 0;
+            L.h = 0;
+            continue;
+        }
+        L.src = offs[l] - base;
+        const double rx = (double)L.w / L.out_w, sx = std::max(rx, 1.0);
+        const double ry = (double)L.h / b.out_h, sy = std::max(ry, 1.0);
+        L.stride_x = (int)std::ceil(2.0 * sx) + 3;
+        L.stride_y = (int)std::ceil(2.0 * sy) + 3;
+        int chunk = rh::kRecThreads;
+        if (rec_span_bound(rx, sx, chunk) > kRecSpanTarget)
+            chunk = (int)std::min<double>(rh::kRecThreads,
+                                          std::max(1.0, std::floor((kRecSpanTarget - 2.0 * sx - 4.0) / rx) + 1.0));
+        L.chunk = chunk;
+        span_cap = (int)std::max<long long>(span_cap, rec_span_bound(rx, sx, chunk));
+        L.coord = n_coords;
+        L.wts = n_wts;
+        n_coords += (long long)L.out_w + b.out_h;
+        n_wts += (long long)L.out_w * L.stride_x + (long long)b.out_h * L.stride_y;
+    }
+}
+
+// Byte range [lo, hi) of the non-empty crops among lines [l0, l1) (lo == hi when none).
+void rec_byte_range(const int64_t* offs, const uint32_t* widths, const uint32_t* heights, int64_t l0, int64_t l1,
+                    int64_t& lo, int64_t& hi) {
+    lo = INT64_MAX;
+    hi = 0;
+    for (int64_t l = l0; l < l1; ++l) {
+        if (widths[l] == 0 || heights[l] == 0) continue;
+        lo = std::min(lo, offs[l]);
+        hi = std::max(hi, offs[l] + (int64_t)widths[l] * (int64_t)heights[l] * 3);
+    }
+    if (lo > hi) lo = hi = 0;
+}
+
+// Lines [l0, l1) of a host-memory batch on one device: crops up in pieces on the copy stream
+// while the previous piece resizes, each piece's rows back to the host as soon as they are done.
+int rec_host_on_slot(rh_ctx* ctx, int slot, const uint8_t* rgb, const int64_t* offs, const uint32_t* widths,
+                     const uint32_t* heights, int64_t l0, int64_t l1, const RecBatch& b, float* out) {
+    if (l1 <= l0) return RH_OK;
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    int64_t b0, b1;
+    rec_byte_range(offs, widths, heights, l0, l1, b0, b1);
+    std::vector<rh::RecLine> lines;
+    long long n_coords, n_wts;
+    int span_cap;
+    rec_describe(offs, widths, heights, l0, l1, b, b0, lines, n_coords, n_wts, span_cap);
+    const int64_t n = l1 - l0;
+    const size_t line_floats = (size_t)3 * b.out_h * b.wmax;
+    RH_CUDA(s.pre_rgb.ensure((size_t)std::max<int64_t>(b1 - b0, 1)));
+    RH_CUDA(s.pre_lines.ensure((size_t)n * sizeof(rh::RecLine)));
+    RH_CUDA(s.pre_coords.ensure((size_t)std::max<long long>(n_coords, 1) * sizeof(int2)));
+    RH_CUDA(s.pre_wts.ensure((size_t)std::max<long long>(n_wts, 1) * sizeof(float)));
+    RH_CUDA(s.pre_out.ensure(std::max<size_t>((size_t)n * line_floats * sizeof(float), 4)));
+    rh::RecParams p{};
+    p.rgb = (const uint8_t*)s.pre_rgb.p;
+    p.lines = (const rh::RecLine*)s.pre_lines.p;
+    p.n_lines = n;
+    p.out_h = (int)b.out_h;
+    p.wmax = (int)b.wmax;
+    p.span_cap = span_cap;
+    p.coords = (int2*)s.pre_coords.p;
+    p.wts = (float*)s.pre_wts.p;
+    p.out = (float*)s.pre_out.p;
+    p.inv = 1.0f / 127.5f;
+    p.status = s.d_status;
+    RH_CUDA(cudaMemcpyAsync(s.pre_lines.p, lines.data(), (size_t)n * sizeof(rh::RecLine), cudaMemcpyHostToDevice,
+                            s.stream));
+    RH_CUDA(rh::launch_rec_weights(p, s.stream));
+    s.launches++;
+    // pieces of about 32 MB of output
+    const int64_t piece = std::max<int64_t>(1, (int64_t)((32u << 20) / std::max<size_t>(line_floats * 4, 1)));
+    const int64_t max_grid_lines = std::max<int64_t>(1, 0x7fffffffLL / b.out_h);
+    const int64_t step = std::min(piece, max_grid_lines);
+    for (int64_t p0 = 0; p0 < n; p0 += step) {
+        const int64_t pn = std::min(step, n - p0);
+        int64_t c0, c1;
+        rec_byte_range(offs, widths, heights, l0 + p0, l0 + p0 + pn, c0, c1);
+        if (c1 > c0) {
+            RH_CUDA(cudaMemcpyAsync((uint8_t*)s.pre_rgb.p + (c0 - b0), rgb + c0, (size_t)(c1 - c0),
+                                    cudaMemcpyHostToDevice, s.copy_stream));
+            RH_CUDA(cudaEventRecord(s.copied, s.copy_stream));
+            RH_CUDA(cudaStreamWaitEvent(s.stream, s.copied, 0));
+        }
+        RH_CUDA(rh::launch_rec_resize(p, p0, pn, s.stream));
+        s.launches++;
+        RH_CUDA(cudaMemcpyAsync(out + (size_t)(l0 + p0) * line_floats, (float*)s.pre_out.p + (size_t)p0 * line_floats,
+                                (size_t)pn * line_floats * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+    }
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    return read_status(s);
 }
 
 }  // namespace
@@ -1011,6 +1195,118 @@ int rh_head_decode_device_noalloc(rh_ctx* ctx, const rh_weight* w, int slot, con
         RH_CUDA(rh::launch_merge(scratch, n_splits, rows, d_idx, d_prob, (cudaStream_t)stream));
         s.launches++;
     }
+    return RH_OK;
+}
+
+// ------------------------------------------------------ recognition preprocessing
+
+uint32_t rh_rec_resized_width(uint32_t orig_w, uint32_t orig_h, uint32_t target_h, uint32_t max_w) {
+    return rec_width(orig_w, orig_h, target_h, max_w);
+}
+
+int rh_rec_batch_shape(const uint32_t* widths, const uint32_t* heights, int64_t n_lines, uint32_t target_h,
+                       uint32_t max_w, uint32_t* out_widths, uint32_t* out_h, uint32_t* out_wmax) {
+    RecBatch b;
+    if (int rc = rec_validate(nullptr, widths, heights, n_lines, target_h, max_w, 0, b)) return rc;
+    if (out_widths && n_lines > 0) std::memcpy(out_widths, b.out_w.data(), (size_t)n_lines * sizeof(uint32_t));
+    if (out_h) *out_h = b.out_h;
+    if (out_wmax) *out_wmax = b.wmax;
+    return RH_OK;
+}
+
+int rh_rec_preprocess(rh_ctx* ctx, const uint8_t* rgb, int64_t rgb_len, const int64_t* rgb_offsets,
+                      const uint32_t* widths, const uint32_t* heights, int64_t n_lines, uint32_t target_h,
+                      uint32_t max_w, float* out, int64_t out_len, uint32_t* out_widths, uint32_t* out_wmax) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (rgb_len < 0) return fail(RH_ERR_INVALID_ARG, "negative pixel buffer length");
+    if (n_lines > 0 && !rgb_offsets) return fail(RH_ERR_INVALID_ARG, "null crop offsets");
+    RecBatch b;
+    if (int rc = rec_validate(rgb_offsets, widths, heights, n_lines, target_h, max_w, rgb_len, b)) return rc;
+    if (out_widths && n_lines > 0) std::memcpy(out_widths, b.out_w.data(), (size_t)n_lines * sizeof(uint32_t));
+    if (out_wmax) *out_wmax = b.wmax;
+    if (n_lines == 0) return RH_OK;
+    const long double need = (long double)n_lines * 3.0L * b.out_h * b.wmax;
+    if (!out || (long double)out_len < need)
+        return fail(RH_ERR_INVALID_ARG, "output holds " + std::to_string(out_len) + " floats; the batch needs " +
+                                            std::to_string((long long)need) + " ([n_lines][3][H][wmax])");
+    if (rgb_len > 0 && !rgb) return fail(RH_ERR_INVALID_ARG, "null pixel buffer");
+    // contiguous line shards of equal size (every line has the same output size), one per device
+    const int nd = (int)ctx->slots.size();
+    std::vector<int64_t> cut(nd + 1);
+    for (int d = 0; d <= nd; ++d) cut[d] = n_lines * d / nd;
+    std::vector<int> rc(nd, RH_OK);
+    std::vector<std::string> msg(nd);
+    auto run = [&](int d) {
+        rc[d] = rec_host_on_slot(ctx, d, rgb, rgb_offsets, widths, heights, cut[d], cut[d + 1], b, out);
+        if (rc[d]) msg[d] = g_err;
+    };
+    if (nd == 1) {
+        run(0);
+    } else {
+        std::vector<std::thread> th;
+        for (int d = 0; d < nd; ++d) th.emplace_back(run, d);
+        for (auto& t : th) t.join();
+    }
+    for (int d = 0; d < nd; ++d)
+        if (rc[d]) return fail(rc[d], msg[d]);
+    return RH_OK;
+}
+
+int rh_rec_preprocess_device(rh_ctx* ctx, int slot, const uint8_t* d_rgb, int64_t rgb_len, const int64_t* rgb_offsets,
+                             const uint32_t* widths, const uint32_t* heights, int64_t n_lines, uint32_t target_h,
+                             uint32_t max_w, float* d_out, int64_t out_len, uint32_t* out_widths, uint32_t* out_wmax,
+                             void* stream) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (slot < 0 || slot >= (int)ctx->slots.size()) return fail(RH_ERR_INVALID_ARG, "slot out of range");
+    if (rgb_len < 0) return fail(RH_ERR_INVALID_ARG, "negative pixel buffer length");
+    if (n_lines > 0 && !rgb_offsets) return fail(RH_ERR_INVALID_ARG, "null crop offsets");
+    RecBatch b;
+    if (int rc = rec_validate(rgb_offsets, widths, heights, n_lines, target_h, max_w, rgb_len, b)) return rc;
+    if (out_widths && n_lines > 0) std::memcpy(out_widths, b.out_w.data(), (size_t)n_lines * sizeof(uint32_t));
+    if (out_wmax) *out_wmax = b.wmax;
+    if (n_lines == 0) return RH_OK;
+    const long double need = (long double)n_lines * 3.0L * b.out_h * b.wmax;
+    if (!d_out || (long double)out_len < need)
+        return fail(RH_ERR_INVALID_ARG, "output holds " + std::to_string(out_len) + " floats; the batch needs " +
+                                            std::to_string((long long)need) + " ([n_lines][3][H][wmax])");
+    if (rgb_len > 0 && !d_rgb) return fail(RH_ERR_INVALID_ARG, "null pixel buffer");
+    if ((long double)n_lines * b.out_h > 2147483647.0L)
+        return fail(RH_ERR_UNSUPPORTED, "n_lines x target height above 2^31 - 1; split the batch");
+    std::vector<rh::RecLine> lines;
+    long long n_coords, n_wts;
+    int span_cap;
+    rec_describe(rgb_offsets, widths, heights, 0, n_lines, b, 0, lines, n_coords, n_wts, span_cap);
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    cudaStream_t st = (cudaStream_t)stream;
+    // Tables are stream-ordered allocations, freed on the same stream after the kernels, so
+    // calls that overlap on other streams never share them.
+    void *d_lines = nullptr, *d_coords = nullptr, *d_wts = nullptr;
+    RH_CUDA(cudaMallocAsync(&d_lines, (size_t)n_lines * sizeof(rh::RecLine), st));
+    RH_CUDA(cudaMallocAsync(&d_coords, (size_t)std::max<long long>(n_coords, 1) * sizeof(int2), st));
+    RH_CUDA(cudaMallocAsync(&d_wts, (size_t)std::max<long long>(n_wts, 1) * sizeof(float), st));
+    rh::RecParams p{};
+    p.rgb = d_rgb;
+    p.lines = (const rh::RecLine*)d_lines;
+    p.n_lines = n_lines;
+    p.out_h = (int)b.out_h;
+    p.wmax = (int)b.wmax;
+    p.span_cap = span_cap;
+    p.coords = (int2*)d_coords;
+    p.wts = (float*)d_wts;
+    p.out = d_out;
+    p.inv = 1.0f / 127.5f;
+    p.status = s.d_status;
+    cudaError_t e = cudaMemcpyAsync(d_lines, lines.data(), (size_t)n_lines * sizeof(rh::RecLine),
+                                    cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = rh::launch_rec_weights(p, st);
+    if (e == cudaSuccess) e = rh::launch_rec_resize(p, 0, n_lines, st);
+    cudaFreeAsync(d_wts, st);
+    cudaFreeAsync(d_coords, st);
+    cudaFreeAsync(d_lines, st);
+    if (e != cudaSuccess) return fail(RH_ERR_CUDA, std::string("recognition preprocessing: ") + cudaGetErrorString(e));
+    s.launches += 2;
     return RH_OK;
 }
 

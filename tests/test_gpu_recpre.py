@@ -1,0 +1,152 @@
+"""GPU parity of the batched recognition preprocessing (rh_rec_preprocess*, the sm_100a
+kernels of recpre_kernels.cu) against the CPU oracle's restatement of RecPreprocess::process
++ build_batch, on identical seeded crops. The resized pixels are bytes before normalisation,
+so the bar is bit-exact: every output float equal."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MIXED = [(100, 30), (40, 40), (900, 20), (10, 60), (0, 5), (7, 0), (1, 1), (300, 48), (65_000, 1), (20, 3000),
+         (8000, 20), (5000, 700), (33, 47), (2, 200), (1500, 64)]
+
+
+@pytest.fixture(scope="module")
+def rh():
+    import rust_ppocrv6_b200 as rh
+
+    rh.load()
+    return rh
+
+
+@pytest.fixture(scope="module")
+def ctx(rh):
+    c = rh.Context()
+    yield c
+    c.close()
+
+
+def crops_of(dims, seed):
+    rng = np.random.default_rng(seed)
+    return [rng.integers(0, 256, (h, w, 3), dtype=np.uint8) for w, h in dims]
+
+
+def assert_same(got, ref, label):
+    assert got.shape == ref.shape, (label, got.shape, ref.shape)
+    bad = got != ref
+    assert not bad.any(), f"[{label}] {bad.sum()} of {bad.size} floats differ; first at {np.argwhere(bad)[0]}"
+
+
+def test_mixed_batch_bit_exact(rh, ctx, oracle):
+    crops = crops_of(MIXED, 11)
+    got, widths = rh.RecPreprocess(ctx=ctx).process_batch(crops)
+    ref, ref_w = oracle.rec_preprocess_batch(crops, threads=4)
+    assert np.array_equal(widths, ref_w)
+    assert_same(got, ref, "mixed")
+    assert ctx.launch_count() > 0
+
+
+@pytest.mark.parametrize("target_h,max_w", [(48, 960), (32, 320), (0, 960), (64, 8), (1, 100)])
+def test_other_heights_and_widths(rh, ctx, oracle, target_h, max_w):
+    crops = crops_of(MIXED[:8] + [(123, 45), (640, 32)], 12 + target_h)
+    got, _ = rh.RecPreprocess(target_h, max_w, ctx=ctx).process_batch(crops)
+    ref, _ = oracle.rec_preprocess_batch(crops, target_h, max_w, threads=4)
+    assert_same(got, ref, f"H={target_h} max_w={max_w}")
+
+
+def test_reference_rec_unit_cases(rh, ctx, oracle):
+    """The cases of src/preprocess/rec.rs:108-182, through the GPU path."""
+    def solid(w, h, rgb=(128, 64, 32)):
+        a = np.zeros((h, w, 3), np.uint8)
+        a[:, :] = rgb
+        return a
+
+    cases = [(solid(100, 10), 48, 8, (1, 3, 48, 32)), (solid(64, 64), 0, 960, (1, 3, 1, 32)),
+             (solid(1000, 10), 48, 200, (1, 3, 48, 200)), (solid(65_000, 1), 48, 960, (1, 3, 48, 960)),
+             (solid(50, 100), 48, 960, (1, 3, 48, 32)), (solid(400, 40, (0, 0, 0)), 48, 960, (1, 3, 48, 480))]
+    for img, th, mw, shape in cases:
+        got = rh.RecPreprocess.with_max_w(th, mw)
+        got.ctx = ctx
+        t = got.process(img)
+        assert t.shape == shape
+        assert_same(t, oracle.rec_preprocess(img, th, mw), f"{img.shape} H={th} max_w={mw}")
+    t = rh.RecPreprocess(ctx=ctx).process(solid(400, 40, (0, 0, 0)))
+    assert np.all(t == -1.0)
+
+
+def test_text_line_batch_bit_exact(rh, ctx, oracle):
+    """The bench's workload shape (every line resized to 48 x 960), 96 lines."""
+    rng = np.random.default_rng(13)
+    hs = rng.integers(24, 65, 96)
+    crops = [rng.integers(0, 256, (int(h), int(20 * h), 3), dtype=np.uint8) for h in hs]
+    got, widths = rh.RecPreprocess(ctx=ctx).process_batch(crops)
+    assert np.all(widths == 960)
+    ref, _ = oracle.rec_preprocess_batch(crops, threads=8)
+    assert_same(got, ref, "text lines")
+
+
+def test_empty_batch_and_empty_crops(rh, ctx, oracle):
+    out, widths = rh.RecPreprocess(ctx=ctx).process_batch([])
+    assert out.shape == (0, 3, 48, 0) and widths.size == 0
+    crops = [np.zeros((0, 10, 3), np.uint8), np.zeros((5, 0, 3), np.uint8)]
+    got, _ = rh.RecPreprocess(ctx=ctx).process_batch(crops)
+    ref, _ = oracle.rec_preprocess_batch(crops)
+    assert_same(got, ref, "empty crops")
+    assert np.all(got[0] == -1.0)
+
+
+def test_device_entry_point(rh, ctx, oracle):
+    import torch
+
+    from rust_ppocrv6_b200.preprocess import _pack_crops
+
+    crops = crops_of(MIXED, 14)
+    blob, offsets, widths, heights = _pack_crops(crops)
+    out_w, h, wmax = rh.batch_shape(widths, heights)
+    d_rgb = torch.from_numpy(blob).to("cuda:0")
+    d_out = torch.full((len(crops) * 3 * h * wmax,), float("nan"), device="cuda:0")
+    stream = torch.cuda.current_stream(0)
+    got_w, got_max = rh.rec_preprocess_device(ctx, d_rgb.data_ptr(), blob.size, offsets, widths, heights,
+                                              d_out.data_ptr(), d_out.numel(), stream=stream.cuda_stream)
+    assert got_max == wmax and np.array_equal(got_w, out_w)
+    stream.synchronize()
+    ctx.sync()
+    ref, _ = oracle.rec_preprocess_batch(crops, threads=4)
+    assert_same(d_out.cpu().numpy().reshape(ref.shape), ref, "device entry point")
+
+
+def test_argument_errors_are_reported_before_any_launch(rh, ctx):
+    import ctypes
+
+    from rust_ppocrv6_b200._lib import load
+    from rust_ppocrv6_b200.preprocess import _p, _pack_crops
+
+    crops = crops_of([(100, 30), (40, 40)], 15)
+    blob, offsets, widths, heights = _pack_crops(crops)
+    lib = load()
+    out = np.empty(2 * 3 * 48 * 480, np.float32)
+    got_w = np.zeros(2, np.uint32)
+    got_max = ctypes.c_uint32(0)
+    before = ctx.launch_count()
+    # short output
+    rc = lib.rh_rec_preprocess(ctx.handle, _p(blob), blob.size, _p(offsets), _p(widths), _p(heights), 2, 48, 960,
+                               _p(out), out.size - 1, _p(got_w), ctypes.byref(got_max))
+    assert rc == rh.RH_ERR_INVALID_ARG and b"needs" in lib.rh_last_error()
+    # a crop that runs past the end of the pixel buffer
+    rc = lib.rh_rec_preprocess(ctx.handle, _p(blob), blob.size - 1, _p(offsets), _p(widths), _p(heights), 2, 48,
+                               960, _p(out), out.size, _p(got_w), ctypes.byref(got_max))
+    assert rc == rh.RH_ERR_INVALID_ARG and b"outside the pixel buffer" in lib.rh_last_error()
+    assert ctx.launch_count() == before
+
+
+def test_sharded_over_every_device(rh, oracle):
+    import torch
+
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("one device")
+    crops = crops_of(MIXED * 3, 16)
+    with rh.Context(list(range(n))) as c:
+        got, _ = rh.RecPreprocess(ctx=c).process_batch(crops)
+    ref, _ = oracle.rec_preprocess_batch(crops, threads=8)
+    assert_same(got, ref, f"{n} devices")
