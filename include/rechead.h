@@ -263,7 +263,7 @@ int rh_rec_batch_shape(const uint32_t *widths, const uint32_t *heights, int64_t 
  * *out_wmax (may be NULL) receive the batch shape. Replaces the per-crop loop
  * `self.rec_preprocess.process(&cropped_patch)` of OcrEngine::recognize
  * (src/pipeline.rs:379) plus build_batch. RH_ERR_INVALID_ARG: a crop outside the pixel
- * buffer, a short output; RH_ERR_UNSUPPORTED: a crop that shrinks by more than 8190x
+ * buffer, a short output; RH_ERR_UNSUPPORTED: a crop that shrinks by more than 6142x
  * horizontally (its filter window would not fit the kernel's shared-memory stage), sizes above
  * the limits of rh_rec_batch_shape.
  */

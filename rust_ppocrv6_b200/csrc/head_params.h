@@ -74,18 +74,21 @@ struct PackParams {
 // Batched recognition preprocessing (recpre_kernels.cu): RecPreprocess::process of each crop
 // (resize to out_h rows with the triangle filter, normalise to [-1, 1]) packed into one
 // [n_lines][3][out_h][wmax] tensor whose columns past a line's width are +1.0 (white).
-constexpr int kRecThreads = 256;   // threads per block; also the most output columns per staged chunk
-constexpr int kRecSpanMax = 16384; // most staged input columns (3 x 16384 f32 = 192 KB of shared memory)
+constexpr int kRecThreads = 256;   // threads per block
+constexpr int kRecSpanMax = 12288; // most staged input columns (float4 each: 192 KB of shared memory)
+constexpr int kRecFastSlots = 8;   // weight slots per output column of a line with kx > 0
 
 struct RecLine {
     long long src;     // byte offset of the crop (RGB8, row-major HWC) in the pixel buffer
     int w, h;          // crop size in pixels; a zero means an empty crop (resized to black)
     int out_w;         // resized width
-    int stride_x;      // weight slots per output column (>= its tap count)
+    int stride_x;      // weight slots per output column (>= its untrimmed tap count)
     int stride_y;      // weight slots per output row
-    int chunk;         // output columns staged at once (1..kRecThreads)
+    int chunk;         // output columns staged at once (1..out_w)
+    int kx;            // 2..4: every column has at most kx non-zero taps (ceil(2 s), s <= 2), its weights
+                       // zero-padded to 4 in a 16-byte aligned slot of kRecFastSlots; 0: general columns
     long long coord;   // first (first tap, tap count) entry: out_w column entries, then out_h row entries
-    long long wts;     // first weight: out_w * stride_x column weights, then out_h * stride_y row weights
+    long long wts;     // first weight (a multiple of 4): out_w * stride_x column weights, then out_h * stride_y
 };
 
 struct RecParams {
@@ -94,8 +97,8 @@ struct RecParams {
     long long n_lines;
     int out_h;           // rows per line (target height, at least 1)
     int wmax;            // columns per line in the output (the largest resized width)
-    int span_cap;        // staged columns (shared memory: 3 x span_cap f32)
-    int2* coords;        // tap windows
+    int span_cap;        // staged columns (shared memory: span_cap float4)
+    int2* coords;        // tap windows, trimmed to their non-zero weights
     float* wts;          // normalised tap weights
     float* out;          // [n_lines][3][out_h][wmax]
     float inv;           // 1 / 127.5 in f32

@@ -408,10 +408,10 @@ int noalloc_scratch(int device, float4** out) {
 }
 
 // ------------------------------------------------------ recognition preprocessing
-// Target staged span when choosing a line's chunk (24 KB of shared memory per block); lines
+// Target staged span when choosing a line's chunk (32 KB of shared memory per block); lines
 // that downscale so much that even one output column needs more than rh::kRecSpanMax input
 // columns are rejected as unsupported.
-constexpr double kRecSpanTarget = 2048.0;
+constexpr double kRecSpanTarget = 2048.0;  // 32 KB of float4
 constexpr uint32_t kRecMaxDim = 1u << 30;   // crop sides above this are rejected
 constexpr uint32_t kRecMaxHeight = 1u << 20;  // target heights above this are rejected
 
@@ -499,15 +499,20 @@ void rec_describe(const int64_t* offs, const uint32_t* widths, const uint32_t* h
         L.src = offs[l] - base;
         const double rx = (double)L.w / L.out_w, sx = std::max(rx, 1.0);
         const double ry = (double)L.h / b.out_h, sy = std::max(ry, 1.0);
-        L.stride_x = (int)std::ceil(2.0 * sx) + 3;
+        // columns of a line that shrinks by at most 2x have at most ceil(2 s) <= 4 non-zero taps
+        // (and at most 2 s + 2 <= 6 before trimming): a padded, 16-byte aligned slot of 8
+        L.kx = sx <= 2.0 ? (int)std::ceil(2.0 * sx) : 0;
+        L.stride_x = L.kx > 0 ? rh::kRecFastSlots : (int)std::ceil(2.0 * sx) + 3;
         L.stride_y = (int)std::ceil(2.0 * sy) + 3;
-        int chunk = rh::kRecThreads;
+        // as many output columns per stage as keep the staged span within the target
+        int chunk = L.out_w;
         if (rec_span_bound(rx, sx, chunk) > kRecSpanTarget)
-            chunk = (int)std::min<double>(rh::kRecThreads,
+            chunk = (int)std::min<double>(L.out_w,
                                           std::max(1.0, std::floor((kRecSpanTarget - 2.0 * sx - 4.0) / rx) + 1.0));
         L.chunk = chunk;
         span_cap = (int)std::max<long long>(span_cap, rec_span_bound(rx, sx, chunk));
         L.coord = n_coords;
+        n_wts = (n_wts + 3) & ~3LL;  // float4 loads of the column weights
         L.wts = n_wts;
         n_coords += (long long)L.out_w + b.out_h;
         n_wts += (long long)L.out_w * L.stride_x + (long long)b.out_h * L.stride_y;

@@ -9,20 +9,28 @@
 // of an n_in -> n_out axis has ratio = n_in / n_out, s = max(ratio, 1), centre (o + 1/2) *
 // ratio, taps [floor(centre - s), ceil(centre + s)) clipped to the image (at least one), tap i
 // weighing max(0, 1 - |(i - (centre - 1/2)) / s|) divided by the f32 sum of the window's
-// weights. Every operation is an IEEE f32 add, multiply or divide in the crate's order
-// (__fadd_rn / __fmul_rn / __fdiv_rn: never contracted into an FMA), so the bytes are those of
-// the crate and the floats those of process().
+// weights; every sum runs over the taps in order. Every operation here is an IEEE f32 add,
+// multiply or divide in that order (__fadd_rn / __fmul_rn / __fdiv_rn: never contracted into
+// an FMA), so the bytes are those of the crate and the floats those of process().
+//
+// Exact shortcuts. Each product is >= +0 (bytes and weights are >= 0), so a running sum never
+// changes when a zero-weight tap is added: the weight tables drop the zero taps at the ends of
+// each window, padded slots carry weight 0, and the first tap's sum 0 + p*w is written p*w.
+// A window's non-zero taps are the integers i with |i - c'| < s, at most ceil(2 s) of them
+// (f32 rounding is monotone, so it never admits a tap the real-valued test rejects).
 //
 // Two launches:
-//   rec_weights_kernel  one block per line: the tap window and normalised weights of each
-//                       output column and row (computed once, reused by every row / column).
-//   rec_resize_kernel   one block per (line, output row y): for chunks of up to 256 output
-//                       columns, the vertical pass of the chunk's input column span into
-//                       shared memory (3 channel planes), then the horizontal pass, one output
-//                       column per thread, writing the three normalised planes (coalesced),
-//                       then the white padding up to wmax. HBM-bound: every crop byte is read
-//                       from DRAM about once (the rows a block shares with its neighbours come
-//                       from L2) and every output float is written once.
+//   rec_weights_kernel  one block per line: the trimmed tap window and normalised weights of
+//                       each output column and row (computed once, reused by every row/column).
+//   rec_resize_kernel   one block per (line, 4 output rows), per row and chunk of output columns (the
+//                       whole line unless its input span is very wide) the vertical pass of the
+//                       chunk's input columns into shared memory (one float4 per column, taps
+//                       unrolled for the row's tap count, weights in registers), then the
+//                       horizontal pass (unrolled to the line's bound kx with float4 weights),
+//                       writing the three normalised planes (coalesced), then the white padding.
+//                       HBM-bound by design: every crop byte is read from DRAM about once (rows
+//                       shared with neighbouring blocks come from L2), every output float is
+//                       written once.
 #include <cstdint>
 
 #include "head_params.h"
@@ -31,10 +39,13 @@ namespace rh {
 
 namespace {
 
+constexpr int kRecRows = 4;  // output rows per block (consecutive: they share input rows and column tables)
+
 __device__ __forceinline__ void flag(int* status) { atomicOr(status, kDevRecPlan); }
 
-// Tap window of output coordinate o (first tap, count) and its normalised weights in w[0..count).
-__device__ int2 tri_window(int n_in, int n_out, int o, int stride, float* __restrict__ w, int* status) {
+// Tap window of output coordinate o, trimmed to its non-zero weights: returns (first tap,
+// count) and leaves the normalised weights in w[0..count), zeros in w[count..pad).
+__device__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, float* __restrict__ w, int* status) {
     const float ratio = __fdiv_rn((float)n_in, (float)n_out);
     const float s = ratio < 1.0f ? 1.0f : ratio;
     const float centre = __fmul_rn(__fadd_rn((float)o, 0.5f), ratio);
@@ -56,14 +67,116 @@ __device__ int2 tri_window(int n_in, int n_out, int o, int stride, float* __rest
         w[j] = wj;
         sum = __fadd_rn(sum, wj);
     }
+    int j0 = 0, j1 = cnt - 1;
     for (int j = 0; j < cnt; ++j) w[j] = __fdiv_rn(w[j], sum);
-    return make_int2((int)lo, cnt);
+    while (j0 < j1 && w[j0] == 0.0f) ++j0;
+    while (j1 > j0 && w[j1] == 0.0f) --j1;
+    const int n = j1 - j0 + 1;
+    if (j0 > 0)
+        for (int j = 0; j < n; ++j) w[j] = w[j + j0];
+    for (int j = n; j < pad && j < stride; ++j) w[j] = 0.0f;
+    return make_int2((int)lo + j0, n);
 }
 
-// Clamp to [0, 255], round half away from zero (the u8 of the resized image), normalise.
+// Clamp to 255 (the sum is never negative), round half away from zero (the u8 of the resized
+// image), normalise.
 __device__ __forceinline__ float to_unit(float t, float inv) {
-    t = t < 0.0f ? 0.0f : (t > 255.0f ? 255.0f : t);
+    t = fminf(t, 255.0f);
     return __fsub_rn(__fmul_rn(roundf(t), inv), 1.0f);
+}
+
+// p * w added to a float4 channel accumulator (the first tap sets it).
+__device__ __forceinline__ void tap(float4& a, float4 p, float w, bool first) {
+    if (first) {
+        a.x = __fmul_rn(p.x, w);
+        a.y = __fmul_rn(p.y, w);
+        a.z = __fmul_rn(p.z, w);
+    } else {
+        a.x = __fadd_rn(a.x, __fmul_rn(p.x, w));
+        a.y = __fadd_rn(a.y, __fmul_rn(p.y, w));
+        a.z = __fadd_rn(a.z, __fmul_rn(p.z, w));
+    }
+}
+
+__device__ __forceinline__ float4 px3(const uint8_t* __restrict__ p) {
+    return make_float4((float)__ldg(p), (float)__ldg(p + 1), (float)__ldg(p + 2), 0.0f);
+}
+
+// Vertical pass of input columns [left0, left0 + span) for a row with NY taps starting at
+// `top` (NY == 0: any count, loop). Each thread takes U columns per step, loading all their
+// bytes before the arithmetic so that the loads overlap.
+template <int NY, int U>
+__device__ __forceinline__ void vpass(float4* __restrict__ vs, const uint8_t* __restrict__ top, size_t pitch,
+                                      int left0, int span, const float* __restrict__ wy, int ny) {
+    if constexpr (NY == 0) {
+        for (int c = threadIdx.x; c < span; c += kRecThreads) {
+            const uint8_t* __restrict__ q = top + (size_t)(left0 + c) * 3;
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < ny; ++j) tap(a, px3(q + j * pitch), __ldg(wy + j), j == 0);
+            vs[c] = a;
+        }
+    } else {
+        float w[NY];
+#pragma unroll
+        for (int j = 0; j < NY; ++j) w[j] = __ldg(wy + j);
+        for (int c0 = threadIdx.x; c0 < span; c0 += U * kRecThreads) {
+            float4 v[U][NY];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = min(c0 + u * kRecThreads, span - 1);  // a clamped column is loaded, not stored
+                const uint8_t* __restrict__ q = top + (size_t)(left0 + c) * 3;
+#pragma unroll
+                for (int j = 0; j < NY; ++j) v[u][j] = px3(q + j * pitch);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int j = 0; j < NY; ++j) tap(a, v[u][j], w[j], j == 0);
+                if (c0 + u * kRecThreads < span) vs[c0 + u * kRecThreads] = a;
+            }
+        }
+    }
+}
+
+// Horizontal pass of output columns [x0, x1): at most KX taps per column (KX == 0: any
+// count). Each thread takes U columns per step, loading their windows first.
+template <int KX, int U>
+__device__ __forceinline__ void hpass(const RecParams& p, const RecLine& L, const float4* __restrict__ vs, int left0,
+                                      int span, int x0, int x1, float* r0, float* r1, float* r2) {
+    const int last = span - 1;
+    for (int xb = x0 + (int)threadIdx.x; xb < x1; xb += U * kRecThreads) {
+        int2 cx[U];
+        float4 w4[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int x = min(xb + u * kRecThreads, x1 - 1);
+            cx[u] = p.coords[L.coord + x];
+            if (KX > 0) w4[u] = __ldg(reinterpret_cast<const float4*>(p.wts + L.wts + (long long)x * L.stride_x));
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int x = xb + u * kRecThreads;
+            if (x >= x1) break;
+            const int base = cx[u].x - left0;
+            if (base < 0 || base + cx[u].y > span) {
+                flag(p.status);
+                continue;
+            }
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (KX > 0 && cx[u].y <= KX) {
+                const float wv[4] = {w4[u].x, w4[u].y, w4[u].z, w4[u].w};
+#pragma unroll
+                for (int j = 0; j < (KX > 0 ? KX : 1); ++j) tap(a, vs[min(base + j, last)], wv[j], j == 0);
+            } else {
+                const float* __restrict__ wx = p.wts + L.wts + (long long)x * L.stride_x;
+                for (int j = 0; j < cx[u].y; ++j) tap(a, vs[base + j], __ldg(wx + j), j == 0);
+            }
+            r0[x] = to_unit(a.x, p.inv);
+            r1[x] = to_unit(a.y, p.inv);
+            r2[x] = to_unit(a.z, p.inv);
+        }
+    }
 }
 
 }  // namespace
@@ -74,11 +187,11 @@ __global__ void __launch_bounds__(kRecThreads) rec_weights_kernel(const RecParam
     const int n = L.out_w + p.out_h;
     for (int j = threadIdx.x; j < n; j += kRecThreads) {
         if (j < L.out_w) {
-            p.coords[L.coord + j] =
-                tri_window(L.w, L.out_w, j, L.stride_x, p.wts + L.wts + (long long)j * L.stride_x, p.status);
+            p.coords[L.coord + j] = tri_window(L.w, L.out_w, j, L.stride_x, L.kx > 0 ? 4 : 0,
+                                               p.wts + L.wts + (long long)j * L.stride_x, p.status);
         } else {
             const int y = j - L.out_w;
-            p.coords[L.coord + j] = tri_window(L.h, p.out_h, y, L.stride_y,
+            p.coords[L.coord + j] = tri_window(L.h, p.out_h, y, L.stride_y, 0,
                                                p.wts + L.wts + (long long)L.out_w * L.stride_x +
                                                    (long long)y * L.stride_y,
                                                p.status);
@@ -86,79 +199,57 @@ __global__ void __launch_bounds__(kRecThreads) rec_weights_kernel(const RecParam
     }
 }
 
-__global__ void __launch_bounds__(kRecThreads) rec_resize_kernel(const RecParams p, long long line0) {
-    extern __shared__ float vs[];  // [3][span_cap]: vertical-pass values of the chunk's input columns
-    const long long li = line0 + blockIdx.x / p.out_h;
-    const int y = (int)(blockIdx.x % p.out_h);
+__global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecParams p, long long line0) {
+    extern __shared__ float4 vs[];  // [span_cap]: vertical-pass values (r, g, b, -) of the chunk's columns
+    const int groups = (p.out_h + kRecRows - 1) / kRecRows;
+    const long long li = line0 + blockIdx.x / groups;
+    const int y0 = (int)(blockIdx.x % groups) * kRecRows, y1 = min(y0 + kRecRows, p.out_h);
     const RecLine L = p.lines[li];
     const size_t plane = (size_t)p.out_h * (size_t)p.wmax;
-    float* r0 = p.out + (size_t)li * 3 * plane + (size_t)y * (size_t)p.wmax;
-    float* r1 = r0 + plane;
-    float* r2 = r1 + plane;
-    for (int x = L.out_w + threadIdx.x; x < p.wmax; x += kRecThreads) {  // white padding (batch_poc.rs:18-19)
-        r0[x] = 1.0f;
-        r1[x] = 1.0f;
-        r2[x] = 1.0f;
-    }
-    if (L.w <= 0 || L.h <= 0) {  // an empty crop resizes to black
-        for (int x = threadIdx.x; x < L.out_w; x += kRecThreads) {
-            r0[x] = -1.0f;
-            r1[x] = -1.0f;
-            r2[x] = -1.0f;
+    float* const line_out = p.out + (size_t)li * 3 * plane;
+    const bool empty = L.w <= 0 || L.h <= 0;
+    for (int y = y0; y < y1; ++y) {  // white padding (batch_poc.rs:18-19); an empty crop is black
+        float* r0 = line_out + (size_t)y * (size_t)p.wmax;
+        for (int x = (empty ? 0 : L.out_w) + threadIdx.x; x < p.wmax; x += kRecThreads) {
+            const float v = x < L.out_w ? -1.0f : 1.0f;
+            r0[x] = v;
+            r0[x + plane] = v;
+            r0[x + 2 * plane] = v;
         }
-        return;
     }
-    const int2 cy = p.coords[L.coord + L.out_w + y];
-    const float* __restrict__ wy = p.wts + L.wts + (long long)L.out_w * L.stride_x + (long long)y * L.stride_y;
+    if (empty) return;
     const size_t pitch = (size_t)L.w * 3;
-    const uint8_t* __restrict__ top = p.rgb + L.src + (size_t)cy.x * pitch;
-    const int cap = p.span_cap;
-    for (int x0 = 0; x0 < L.out_w; x0 += L.chunk) {
-        const int x1 = min(x0 + L.chunk, L.out_w);
-        const int2 a = p.coords[L.coord + x0], b = p.coords[L.coord + x1 - 1];
-        const int left0 = a.x, span = b.x + b.y - a.x;
-        if (span <= 0 || span > cap) {  // same values in every thread: the whole block leaves
-            if (threadIdx.x == 0) flag(p.status);
-            return;
-        }
-        // vertical pass over input columns [left0, left0 + span): taps in order, f32
-        for (int c = threadIdx.x; c < span; c += kRecThreads) {
-            const uint8_t* __restrict__ px = top + (size_t)(left0 + c) * 3;
-            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f;
-            for (int i = 0; i < cy.y; ++i) {
-                const float wv = __ldg(wy + i);
-                a0 = __fadd_rn(a0, __fmul_rn((float)__ldg(px), wv));
-                a1 = __fadd_rn(a1, __fmul_rn((float)__ldg(px + 1), wv));
-                a2 = __fadd_rn(a2, __fmul_rn((float)__ldg(px + 2), wv));
-                px += pitch;
+    for (int y = y0; y < y1; ++y) {
+        const int2 cy = p.coords[L.coord + L.out_w + y];
+        const float* __restrict__ wy = p.wts + L.wts + (long long)L.out_w * L.stride_x + (long long)y * L.stride_y;
+        const uint8_t* __restrict__ top = p.rgb + L.src + (size_t)cy.x * pitch;
+        float* r0 = line_out + (size_t)y * (size_t)p.wmax;
+        float* r1 = r0 + plane;
+        float* r2 = r1 + plane;
+        for (int x0 = 0; x0 < L.out_w; x0 += L.chunk) {
+            const int x1 = min(x0 + L.chunk, L.out_w);
+            const int2 a = p.coords[L.coord + x0], b = p.coords[L.coord + x1 - 1];
+            const int left0 = a.x, span = b.x + b.y - a.x;
+            if (span <= 0 || span > p.span_cap) {  // same values in every thread: the whole block leaves
+                if (threadIdx.x == 0) flag(p.status);
+                return;
             }
-            vs[c] = a0;
-            vs[cap + c] = a1;
-            vs[2 * cap + c] = a2;
-        }
-        __syncthreads();
-        // horizontal pass: one output column per thread
-        const int x = x0 + (int)threadIdx.x;
-        if (x < x1) {
-            const int2 cx = p.coords[L.coord + x];
-            const float* __restrict__ wx = p.wts + L.wts + (long long)x * L.stride_x;
-            const int base = cx.x - left0;
-            if (base >= 0 && base + cx.y <= span) {
-                float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f;
-                for (int j = 0; j < cx.y; ++j) {
-                    const float wv = __ldg(wx + j);
-                    t0 = __fadd_rn(t0, __fmul_rn(vs[base + j], wv));
-                    t1 = __fadd_rn(t1, __fmul_rn(vs[cap + base + j], wv));
-                    t2 = __fadd_rn(t2, __fmul_rn(vs[2 * cap + base + j], wv));
-                }
-                r0[x] = to_unit(t0, p.inv);
-                r1[x] = to_unit(t1, p.inv);
-                r2[x] = to_unit(t2, p.inv);
-            } else {
-                flag(p.status);
+            if (y > y0 || x0 > 0) __syncthreads();  // the previous horizontal pass is done with the stage
+            switch (cy.y) {
+                case 1: vpass<1, 2>(vs, top, pitch, left0, span, wy, 1); break;
+                case 2: vpass<2, 2>(vs, top, pitch, left0, span, wy, 2); break;
+                case 3: vpass<3, 2>(vs, top, pitch, left0, span, wy, 3); break;
+                case 4: vpass<4, 1>(vs, top, pitch, left0, span, wy, 4); break;
+                default: vpass<0, 1>(vs, top, pitch, left0, span, wy, cy.y); break;
+            }
+            __syncthreads();
+            switch (L.kx) {
+                case 2: hpass<2, 2>(p, L, vs, left0, span, x0, x1, r0, r1, r2); break;
+                case 3: hpass<3, 2>(p, L, vs, left0, span, x0, x1, r0, r1, r2); break;
+                case 4: hpass<4, 2>(p, L, vs, left0, span, x0, x1, r0, r1, r2); break;
+                default: hpass<0, 1>(p, L, vs, left0, span, x0, x1, r0, r1, r2); break;
             }
         }
-        __syncthreads();
     }
 }
 
@@ -170,12 +261,13 @@ cudaError_t launch_rec_weights(const RecParams& p, cudaStream_t stream) {
 
 cudaError_t launch_rec_resize(const RecParams& p, long long line0, long long n, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
-    const size_t smem = (size_t)3 * (size_t)p.span_cap * sizeof(float);
+    const size_t smem = (size_t)p.span_cap * sizeof(float4);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(rec_resize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    rec_resize_kernel<<<(unsigned)(n * p.out_h), kRecThreads, smem, stream>>>(p, line0);
+    const long long groups = (p.out_h + kRecRows - 1) / kRecRows;
+    rec_resize_kernel<<<(unsigned)(n * groups), kRecThreads, smem, stream>>>(p, line0);
     return cudaGetLastError();
 }
 

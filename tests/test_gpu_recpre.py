@@ -124,7 +124,8 @@ def test_argument_errors_are_reported_before_any_launch(rh, ctx):
     crops = crops_of([(100, 30), (40, 40)], 15)
     blob, offsets, widths, heights = _pack_crops(crops)
     lib = load()
-    out = np.empty(2 * 3 * 48 * 480, np.float32)
+    _, h, wmax = rh.batch_shape(widths, heights)
+    out = np.empty(2 * 3 * h * wmax, np.float32)
     got_w = np.zeros(2, np.uint32)
     got_max = ctypes.c_uint32(0)
     before = ctx.launch_count()
