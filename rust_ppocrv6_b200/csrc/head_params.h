@@ -77,6 +77,7 @@ struct PackParams {
 constexpr int kRecThreads = 256;   // threads per block
 constexpr int kRecSpanMax = 12288; // most staged input columns (float4 each: 192 KB of shared memory)
 constexpr int kRecFastSlots = 8;   // weight slots per output column of a line with kx > 0
+constexpr int kRecMetaMax = 4096;  // most column windows staged per block (80 KB)
 
 struct RecLine {
     long long src;     // byte offset of the crop (RGB8, row-major HWC) in the pixel buffer
@@ -98,6 +99,8 @@ struct RecParams {
     int out_h;           // rows per line (target height, at least 1)
     int wmax;            // columns per line in the output (the largest resized width)
     int span_cap;        // staged columns (shared memory: span_cap float4)
+    int meta_cap;        // column windows staged per block (0: none; lines with kx > 0, one chunk and
+                         // out_w <= meta_cap stage theirs: int + float4 each)
     int2* coords;        // tap windows, trimmed to their non-zero weights
     float* wts;          // normalised tap weights
     float* out;          // [n_lines][3][out_h][wmax]

@@ -66,6 +66,7 @@ struct Slot {
     DevBuf a, idx, prob, out, partial;
     DevBuf lines, tok_off, tokens, scores;  // CTC collapse on the device
     DevBuf pre_rgb, pre_lines, pre_coords, pre_wts, pre_out;  // recognition preprocessing
+    cudaEvent_t pre_done = nullptr;  // recorded after the last kernel that reads pre_lines/coords/wts
     std::mutex mu;
     int64_t launches = 0;
     // Frees everything, also on a context whose creation failed part-way.
@@ -78,6 +79,7 @@ struct Slot {
             b->release();
         if (d_status) cudaFree(d_status);
         if (copied) cudaEventDestroy(copied);
+        if (pre_done) cudaEventDestroy(pre_done);
         if (copy_stream) cudaStreamDestroy(copy_stream);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -479,11 +481,12 @@ int rec_validate(const int64_t* offs, const uint32_t* widths, const uint32_t* he
 // tables are laid out from 0. span_cap receives the largest staged span the lines need.
 void rec_describe(const int64_t* offs, const uint32_t* widths, const uint32_t* heights, int64_t l0, int64_t l1,
                   const RecBatch& b, int64_t base, std::vector<rh::RecLine>& lines, long long& n_coords,
-                  long long& n_wts, int& span_cap) {
+                  long long& n_wts, int& span_cap, int& meta_cap) {
     lines.resize((size_t)(l1 - l0));
     n_coords = 0;
     n_wts = 0;
     span_cap = 1;
+    meta_cap = 0;
     for (int64_t l = l0; l < l1; ++l) {
         rh::RecLine& L = lines[l - l0];
         L = rh::RecLine{};
@@ -511,12 +514,18 @@ void rec_describe(const int64_t* offs, const uint32_t* widths, const uint32_t* h
                                           std::max(1.0, std::floor((kRecSpanTarget - 2.0 * sx - 4.0) / rx) + 1.0));
         L.chunk = chunk;
         span_cap = (int)std::max<long long>(span_cap, rec_span_bound(rx, sx, chunk));
+        if (L.kx > 0 && chunk == L.out_w && L.out_w <= rh::kRecMetaMax) {
+            meta_cap = std::max(meta_cap, L.out_w);
+            span_cap = (int)std::max<long long>(span_cap, rec_span_bound(rx, sx, chunk) + 4);  // tap padding
+        }
         L.coord = n_coords;
         n_wts = (n_wts + 3) & ~3LL;  // float4 loads of the column weights
         L.wts = n_wts;
         n_coords += (long long)L.out_w + b.out_h;
         n_wts += (long long)L.out_w * L.stride_x + (long long)b.out_h * L.stride_y;
     }
+    // the staged windows share the block's shared memory with the span stage (227 KB per block)
+    if ((long long)span_cap * 16 + (long long)meta_cap * 20 > 200 * 1024) meta_cap = 0;
 }
 
 // Byte range [lo, hi) of the non-empty crops among lines [l0, l1) (lo == hi when none).
@@ -532,6 +541,18 @@ void rec_byte_range(const int64_t* offs, const uint32_t* widths, const uint32_t*
     if (lo > hi) lo = hi = 0;
 }
 
+// Makes the slot's line/tap tables hold n lines, n_coords windows and n_wts weights, and orders
+// `stream` after every kernel of the previous preprocessing call on this slot (whatever its
+// stream), so that the tables are not overwritten while that call still reads them.
+int rec_tables(Slot& s, cudaStream_t stream, int64_t n, long long n_coords, long long n_wts) {
+    if (!s.pre_done) RH_CUDA(cudaEventCreateWithFlags(&s.pre_done, cudaEventDisableTiming));
+    RH_CUDA(cudaStreamWaitEvent(stream, s.pre_done, 0));
+    RH_CUDA(s.pre_lines.ensure((size_t)std::max<int64_t>(n, 1) * sizeof(rh::RecLine)));
+    RH_CUDA(s.pre_coords.ensure((size_t)std::max<long long>(n_coords, 1) * sizeof(int2)));
+    RH_CUDA(s.pre_wts.ensure((size_t)std::max<long long>(n_wts, 1) * sizeof(float)));
+    return RH_OK;
+}
+
 // Lines [l0, l1) of a host-memory batch on one device: crops up in pieces on the copy stream
 // while the previous piece resizes, each piece's rows back to the host as soon as they are done.
 int rec_host_on_slot(rh_ctx* ctx, int slot, const uint8_t* rgb, const int64_t* offs, const uint32_t* widths,
@@ -544,14 +565,12 @@ int rec_host_on_slot(rh_ctx* ctx, int slot, const uint8_t* rgb, const int64_t* o
     rec_byte_range(offs, widths, heights, l0, l1, b0, b1);
     std::vector<rh::RecLine> lines;
     long long n_coords, n_wts;
-    int span_cap;
-    rec_describe(offs, widths, heights, l0, l1, b, b0, lines, n_coords, n_wts, span_cap);
+    int span_cap, meta_cap;
+    rec_describe(offs, widths, heights, l0, l1, b, b0, lines, n_coords, n_wts, span_cap, meta_cap);
     const int64_t n = l1 - l0;
     const size_t line_floats = (size_t)3 * b.out_h * b.wmax;
+    if (int rc = rec_tables(s, s.stream, n, n_coords, n_wts)) return rc;
     RH_CUDA(s.pre_rgb.ensure((size_t)std::max<int64_t>(b1 - b0, 1)));
-    RH_CUDA(s.pre_lines.ensure((size_t)n * sizeof(rh::RecLine)));
-    RH_CUDA(s.pre_coords.ensure((size_t)std::max<long long>(n_coords, 1) * sizeof(int2)));
-    RH_CUDA(s.pre_wts.ensure((size_t)std::max<long long>(n_wts, 1) * sizeof(float)));
     RH_CUDA(s.pre_out.ensure(std::max<size_t>((size_t)n * line_floats * sizeof(float), 4)));
     rh::RecParams p{};
     p.rgb = (const uint8_t*)s.pre_rgb.p;
@@ -560,6 +579,7 @@ int rec_host_on_slot(rh_ctx* ctx, int slot, const uint8_t* rgb, const int64_t* o
     p.out_h = (int)b.out_h;
     p.wmax = (int)b.wmax;
     p.span_cap = span_cap;
+    p.meta_cap = meta_cap;
     p.coords = (int2*)s.pre_coords.p;
     p.wts = (float*)s.pre_wts.p;
     p.out = (float*)s.pre_out.p;
@@ -588,6 +608,7 @@ int rec_host_on_slot(rh_ctx* ctx, int slot, const uint8_t* rgb, const int64_t* o
         RH_CUDA(cudaMemcpyAsync(out + (size_t)(l0 + p0) * line_floats, (float*)s.pre_out.p + (size_t)p0 * line_floats,
                                 (size_t)pn * line_floats * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
     }
+    RH_CUDA(cudaEventRecord(s.pre_done, s.stream));
     RH_CUDA(cudaStreamSynchronize(s.stream));
     return read_status(s);
 }
@@ -1279,38 +1300,31 @@ int rh_rec_preprocess_device(rh_ctx* ctx, int slot, const uint8_t* d_rgb, int64_
         return fail(RH_ERR_UNSUPPORTED, "n_lines x target height above 2^31 - 1; split the batch");
     std::vector<rh::RecLine> lines;
     long long n_coords, n_wts;
-    int span_cap;
-    rec_describe(rgb_offsets, widths, heights, 0, n_lines, b, 0, lines, n_coords, n_wts, span_cap);
+    int span_cap, meta_cap;
+    rec_describe(rgb_offsets, widths, heights, 0, n_lines, b, 0, lines, n_coords, n_wts, span_cap, meta_cap);
     Slot& s = *ctx->slots[slot];
     std::lock_guard<std::mutex> lock(s.mu);
     RH_CUDA(cudaSetDevice(s.device));
     cudaStream_t st = (cudaStream_t)stream;
-    // Tables are stream-ordered allocations, freed on the same stream after the kernels, so
-    // calls that overlap on other streams never share them.
-    void *d_lines = nullptr, *d_coords = nullptr, *d_wts = nullptr;
-    RH_CUDA(cudaMallocAsync(&d_lines, (size_t)n_lines * sizeof(rh::RecLine), st));
-    RH_CUDA(cudaMallocAsync(&d_coords, (size_t)std::max<long long>(n_coords, 1) * sizeof(int2), st));
-    RH_CUDA(cudaMallocAsync(&d_wts, (size_t)std::max<long long>(n_wts, 1) * sizeof(float), st));
+    if (int rc = rec_tables(s, st, n_lines, n_coords, n_wts)) return rc;
     rh::RecParams p{};
     p.rgb = d_rgb;
-    p.lines = (const rh::RecLine*)d_lines;
+    p.lines = (const rh::RecLine*)s.pre_lines.p;
     p.n_lines = n_lines;
     p.out_h = (int)b.out_h;
     p.wmax = (int)b.wmax;
     p.span_cap = span_cap;
-    p.coords = (int2*)d_coords;
-    p.wts = (float*)d_wts;
+    p.meta_cap = meta_cap;
+    p.coords = (int2*)s.pre_coords.p;
+    p.wts = (float*)s.pre_wts.p;
     p.out = d_out;
     p.inv = 1.0f / 127.5f;
     p.status = s.d_status;
-    cudaError_t e = cudaMemcpyAsync(d_lines, lines.data(), (size_t)n_lines * sizeof(rh::RecLine),
-                                    cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = rh::launch_rec_weights(p, st);
-    if (e == cudaSuccess) e = rh::launch_rec_resize(p, 0, n_lines, st);
-    cudaFreeAsync(d_wts, st);
-    cudaFreeAsync(d_coords, st);
-    cudaFreeAsync(d_lines, st);
-    if (e != cudaSuccess) return fail(RH_ERR_CUDA, std::string("recognition preprocessing: ") + cudaGetErrorString(e));
+    RH_CUDA(cudaMemcpyAsync(s.pre_lines.p, lines.data(), (size_t)n_lines * sizeof(rh::RecLine), cudaMemcpyHostToDevice,
+                            st));
+    RH_CUDA(rh::launch_rec_weights(p, st));
+    RH_CUDA(rh::launch_rec_resize(p, 0, n_lines, st));
+    RH_CUDA(cudaEventRecord(s.pre_done, st));
     s.launches += 2;
     return RH_OK;
 }
