@@ -474,6 +474,8 @@ int rec_validate(const int64_t* offs, const uint32_t* widths, const uint32_t* he
                                                 std::to_string(rh::kRecSpanMax / 2 - 2) +
                                                 "x horizontally; split it or pre-scale it");
     }
+    if ((uint64_t)b.wmax + b.out_h > 65535ull * rh::kRecThreads)
+        return fail(RH_ERR_UNSUPPORTED, "resized width + target height above 16,776,960");
     return RH_OK;
 }
 

@@ -20,8 +20,8 @@
 // (f32 rounding is monotone, so it never admits a tap the real-valued test rejects).
 //
 // Two launches:
-//   rec_weights_kernel  one block per line: the trimmed tap window and normalised weights of
-//                       each output column and row (computed once, reused by every row/column).
+//   rec_weights_kernel  one thread per (line, output column or row): the trimmed tap window and
+//                       normalised weights (computed once, reused by every row / column).
 //   rec_resize_kernel   one block per (line, 8 output rows). The white padding first; then per
 //                       row and chunk of output columns (the whole line unless its input span is
 //                       very wide): the vertical pass of the chunk's input columns into shared
@@ -216,18 +216,15 @@ __device__ __forceinline__ void hpass_staged(const float4* __restrict__ vs, cons
 __global__ void __launch_bounds__(kRecThreads) rec_weights_kernel(const RecParams p) {
     const RecLine L = p.lines[blockIdx.x];
     if (L.w <= 0 || L.h <= 0) return;  // empty crop: black, no taps
-    const int n = L.out_w + p.out_h;
-    for (int j = threadIdx.x; j < n; j += kRecThreads) {
-        if (j < L.out_w) {
-            p.coords[L.coord + j] = tri_window(L.w, L.out_w, j, L.stride_x, L.kx > 0 ? 4 : 0,
-                                               p.wts + L.wts + (long long)j * L.stride_x, p.status);
-        } else {
-            const int y = j - L.out_w;
-            p.coords[L.coord + j] = tri_window(L.h, p.out_h, y, L.stride_y, 0,
-                                               p.wts + L.wts + (long long)L.out_w * L.stride_x +
-                                                   (long long)y * L.stride_y,
-                                               p.status);
-        }
+    const int j = blockIdx.y * kRecThreads + threadIdx.x;  // output column j, or row j - out_w
+    if (j < L.out_w) {
+        p.coords[L.coord + j] = tri_window(L.w, L.out_w, j, L.stride_x, L.kx > 0 ? 4 : 0,
+                                           p.wts + L.wts + (long long)j * L.stride_x, p.status);
+    } else if (j < L.out_w + p.out_h) {
+        const int y = j - L.out_w;
+        p.coords[L.coord + j] = tri_window(L.h, p.out_h, y, L.stride_y, 0,
+                                           p.wts + L.wts + (long long)L.out_w * L.stride_x + (long long)y * L.stride_y,
+                                           p.status);
     }
 }
 
@@ -332,7 +329,8 @@ __global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecPar
 
 cudaError_t launch_rec_weights(const RecParams& p, cudaStream_t stream) {
     if (p.n_lines <= 0) return cudaSuccess;
-    rec_weights_kernel<<<(unsigned)p.n_lines, kRecThreads, 0, stream>>>(p);
+    const dim3 grid((unsigned)p.n_lines, (unsigned)((p.wmax + p.out_h + kRecThreads - 1) / kRecThreads));
+    rec_weights_kernel<<<grid, kRecThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -51,3 +51,19 @@ def test_bench_helpers():
     t = bench.profiled_traffic()
     assert t is None or t > 60_000_000  # DRAM bytes of one cfg2 launch from the committed ncu summary
     assert np.all(np.diff(off) >= 0)
+
+
+def test_reference_arm_for_preprocessing():
+    rec = _run("--impl", "reference", "--workload", "recpre", "--steps", "1", "--warmup", "0",
+               "--cpu-sample-lines", "8")
+    assert rec["impl"] == "reference" and rec["unit"] == "lines/s" and rec["value"] > 0
+    assert rec["cpu_baseline"]["kind"] == "port" and rec["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_preprocessing_workload():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    blob, offsets, widths, heights = bench.recpre_workload(0, n_lines=16)
+    assert np.all(widths == 20 * heights) and np.all((heights >= 24) & (heights <= 64))
+    assert offsets[0] == 0 and int(offsets[-1]) + int(widths[-1]) * int(heights[-1]) * 3 == blob.size
