@@ -151,3 +151,65 @@ def test_sharded_over_every_device(rh, oracle):
         got, _ = rh.RecPreprocess(ctx=c).process_batch(crops)
     ref, _ = oracle.rec_preprocess_batch(crops, threads=8)
     assert_same(got, ref, f"{n} devices")
+
+
+def test_crops_out_of_order_shared_and_in_a_larger_buffer(rh, ctx, oracle):
+    """Offsets need not follow line order: crops stored backwards, one crop used twice, and
+    unrelated bytes around them in the pixel buffer."""
+    import ctypes
+
+    from rust_ppocrv6_b200._lib import load
+    from rust_ppocrv6_b200.preprocess import _p
+
+    dims = [(120, 33), (64, 50), (9, 2), (300, 60)]
+    crops = crops_of(dims, 17)
+    rng = np.random.default_rng(18)
+    parts, offs = [rng.integers(0, 256, 37, dtype=np.uint8)], {}
+    pos = 37
+    for i in reversed(range(len(crops))):
+        offs[i] = pos
+        parts.append(crops[i].reshape(-1))
+        pos += crops[i].size
+        parts.append(rng.integers(0, 256, 11, dtype=np.uint8))
+        pos += 11
+    blob = np.concatenate(parts)
+    order = [0, 1, 2, 3, 1]  # line 4 reuses crop 1's bytes
+    offsets = np.array([offs[i] for i in order], np.int64)
+    widths = np.array([dims[i][0] for i in order], np.uint32)
+    heights = np.array([dims[i][1] for i in order], np.uint32)
+    _, h, wmax = rh.batch_shape(widths, heights)
+    out = np.empty((len(order), 3, h, wmax), np.float32)
+    got_w = np.zeros(len(order), np.uint32)
+    got_max = ctypes.c_uint32(0)
+    rc = load().rh_rec_preprocess(ctx.handle, _p(blob), blob.size, _p(offsets), _p(widths), _p(heights), len(order),
+                                  48, 960, _p(out), out.size, _p(got_w), ctypes.byref(got_max))
+    assert rc == 0, load().rh_last_error()
+    ref, _ = oracle.rec_preprocess_batch([crops[i] for i in order])
+    assert_same(out, ref, "out of order")
+
+
+def test_many_lines_run_in_pieces(rh, ctx, oracle):
+    """600 lines: the host path cuts the batch into pieces of ~32 MB of output (58 lines at
+    48 x 960) whose copies overlap the resize; every piece must land in its place."""
+    rng = np.random.default_rng(19)
+    hs = rng.integers(8, 90, 600)
+    ws = rng.integers(1, 1400, 600)
+    crops = [rng.integers(0, 256, (int(h), int(w), 3), dtype=np.uint8) for w, h in zip(ws, hs)]
+    got, widths = rh.RecPreprocess(ctx=ctx).process_batch(crops)
+    ref, ref_w = oracle.rec_preprocess_batch(crops, threads=8)
+    assert np.array_equal(widths, ref_w)
+    assert_same(got, ref, "600 lines")
+
+
+def test_concurrent_callers_share_a_context(rh, ctx, oracle):
+    """The engine calls preprocessing from several worker threads; calls on one context are
+    serialised per device and each gets its own result."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    batches = [crops_of(MIXED[:6] + [(200 + 10 * i, 40)], 20 + i) for i in range(6)]
+    pre = rh.RecPreprocess(ctx=ctx)
+    with ThreadPoolExecutor(6) as ex:
+        results = list(ex.map(pre.process_batch, batches))
+    for i, (got, _) in enumerate(results):
+        ref, _ = oracle.rec_preprocess_batch(batches[i])
+        assert_same(got, ref, f"thread {i}")
