@@ -48,6 +48,8 @@ __device__ __forceinline__ void flag(int* status) { atomicOr(status, kDevRecPlan
 
 // Tap window of output coordinate o, trimmed to its non-zero weights: returns (first tap,
 // count) and leaves the normalised weights in w[0..count), zeros in w[count..pad).
+// Windows of up to 8 taps (every axis that shrinks by at most 3x) are computed in registers
+// and written once; wider ones go through w itself.
 __device__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, float* __restrict__ w, int* status) {
     const float ratio = __fdiv_rn((float)n_in, (float)n_out);
     const float s = ratio < 1.0f ? 1.0f : ratio;
@@ -64,6 +66,31 @@ __device__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, floa
     }
     const float c0 = __fsub_rn(centre, 0.5f);
     float sum = 0.0f;
+    if (cnt <= 8) {
+        float r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float x = fabsf(__fdiv_rn(__fsub_rn((float)(lo + j), c0), s));
+            r[j] = (j < cnt && x < 1.0f) ? __fsub_rn(1.0f, x) : 0.0f;
+            sum = __fadd_rn(sum, r[j]);  // taps past cnt add +0: the sum is unchanged
+        }
+        int j0 = cnt, j1 = -1;  // first and last non-zero tap
+#pragma unroll
+        for (int j = 7; j >= 0; --j) j0 = r[j] != 0.0f ? j : j0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) j1 = r[j] != 0.0f ? j : j1;
+        if (j1 < j0) j0 = j1 = 0;  // no non-zero tap (a zero sum; never expected): keep one
+        const int n = j1 - j0 + 1;
+        const int m = max(n, min(pad, stride));  // slots to write
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float v = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v = (j == k + j0) ? r[j] : v;
+            if (k < m) w[k] = k < n ? __fdiv_rn(v, sum) : 0.0f;
+        }
+        return make_int2((int)lo + j0, n);
+    }
     for (int j = 0; j < cnt; ++j) {
         const float x = fabsf(__fdiv_rn(__fsub_rn((float)(lo + j), c0), s));
         const float wj = x < 1.0f ? __fsub_rn(1.0f, x) : 0.0f;
