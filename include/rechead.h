@@ -156,7 +156,8 @@ int rh_head_decode_kt_device(rh_ctx *ctx, const rh_weight *w, int slot, const fl
                              int64_t t_len, int32_t *d_idx, float *d_prob, void *stream);
 
 /* Device-memory forms on context device `slot` (0-based) and `stream` (cudaStream_t, NULL =
- * the legacy default stream). Asynchronous; failures surface at rh_sync(). */
+ * the legacy default stream). Asynchronous; failures surface at rh_sync(). Calls on one slot
+ * from different streams are ordered on the slot's scratch by an event, so they never race. */
 int rh_head_decode_device(rh_ctx *ctx, const rh_weight *w, int slot, const float *d_a, int64_t rows, int32_t *d_idx,
                           float *d_prob, void *stream);
 int rh_matmul_quantized_b_device(rh_ctx *ctx, const rh_weight *w, int slot, const float *d_a, int64_t rows,

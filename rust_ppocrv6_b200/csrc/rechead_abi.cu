@@ -67,6 +67,7 @@ struct Slot {
     DevBuf lines, tok_off, tokens, scores;  // CTC collapse on the device
     DevBuf pre_rgb, pre_lines, pre_coords, pre_wts, pre_out;  // recognition preprocessing
     cudaEvent_t pre_done = nullptr;  // recorded after the last kernel that reads pre_lines/coords/wts
+    cudaEvent_t part_done = nullptr;  // recorded after the last merge that reads `partial`
     std::mutex mu;
     int64_t launches = 0;
     // Frees everything, also on a context whose creation failed part-way.
@@ -80,6 +81,7 @@ struct Slot {
         if (d_status) cudaFree(d_status);
         if (copied) cudaEventDestroy(copied);
         if (pre_done) cudaEventDestroy(pre_done);
+        if (part_done) cudaEventDestroy(part_done);
         if (copy_stream) cudaStreamDestroy(copy_stream);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -219,7 +221,14 @@ int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per&
     p.debug_flags = 0;
     if (const char* dbg = std::getenv("RH_DEBUG_FLAGS")) p.debug_flags = std::atoi(dbg);
     if (!emit_logits && n_splits > 1) {
-        RH_CUDA(s.partial.ensure((size_t)n_splits * (size_t)rows * sizeof(float4)));
+        // The split scratch is the slot's: order this call after the previous merge that read
+        // it (which may run on another caller stream), and let that merge finish before the
+        // buffer is reallocated.
+        if (!s.part_done) RH_CUDA(cudaEventCreateWithFlags(&s.part_done, cudaEventDisableTiming));
+        const size_t need = (size_t)n_splits * (size_t)rows * sizeof(float4);
+        if (need > s.partial.cap) RH_CUDA(cudaEventSynchronize(s.part_done));
+        RH_CUDA(s.partial.ensure(need));
+        RH_CUDA(cudaStreamWaitEvent(stream, s.part_done, 0));
         p.partial = static_cast<float4*>(s.partial.p);
     }
     RH_CUDA(rh::launch_head(p, emit_logits, grid, stream));
@@ -227,6 +236,7 @@ int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per&
     if (!emit_logits && n_splits > 1) {
         RH_CUDA(rh::launch_merge(p.partial, n_splits, rows, d_idx, d_prob, stream));
         s.launches++;
+        RH_CUDA(cudaEventRecord(s.part_done, stream));
     }
     return RH_OK;
 }
@@ -548,10 +558,15 @@ void rec_byte_range(const int64_t* offs, const uint32_t* widths, const uint32_t*
 // stream), so that the tables are not overwritten while that call still reads them.
 int rec_tables(Slot& s, cudaStream_t stream, int64_t n, long long n_coords, long long n_wts) {
     if (!s.pre_done) RH_CUDA(cudaEventCreateWithFlags(&s.pre_done, cudaEventDisableTiming));
+    const size_t b_lines = (size_t)std::max<int64_t>(n, 1) * sizeof(rh::RecLine);
+    const size_t b_coords = (size_t)std::max<long long>(n_coords, 1) * sizeof(int2);
+    const size_t b_wts = (size_t)std::max<long long>(n_wts, 1) * sizeof(float);
+    if (b_lines > s.pre_lines.cap || b_coords > s.pre_coords.cap || b_wts > s.pre_wts.cap)
+        RH_CUDA(cudaEventSynchronize(s.pre_done));  // the old buffers are freed below
     RH_CUDA(cudaStreamWaitEvent(stream, s.pre_done, 0));
-    RH_CUDA(s.pre_lines.ensure((size_t)std::max<int64_t>(n, 1) * sizeof(rh::RecLine)));
-    RH_CUDA(s.pre_coords.ensure((size_t)std::max<long long>(n_coords, 1) * sizeof(int2)));
-    RH_CUDA(s.pre_wts.ensure((size_t)std::max<long long>(n_wts, 1) * sizeof(float)));
+    RH_CUDA(s.pre_lines.ensure(b_lines));
+    RH_CUDA(s.pre_coords.ensure(b_coords));
+    RH_CUDA(s.pre_wts.ensure(b_wts));
     return RH_OK;
 }
 

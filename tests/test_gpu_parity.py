@@ -527,6 +527,39 @@ def test_device_pointer_entry_points_match_host(rh, ctx):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), logits_h.view(np.uint32))
 
 
+def test_device_calls_on_two_streams_share_the_slot_safely(rh, ctx):
+    """Two device-form calls on one slot from different caller streams, back to back with no
+    synchronisation: both use the slot's split scratch (few rows -> the class range is split),
+    and an event orders them on it, so each gets exactly its synchronous result."""
+    import torch
+
+    from rust_ppocrv6_b200 import workloads
+
+    wl = workloads.make(1, scale=0.5)
+    qw = rh.QuantizedWeight.from_f32_transposed(wl.w_t, ctx=ctx, bias=wl.bias)
+    rows = min(wl.rows, 1500)
+    xa = np.ascontiguousarray(wl.x[:rows])
+    xb = np.ascontiguousarray(wl.x[:rows][::-1])
+    ref = [rh.head_decode(x, qw) for x in (xa, xb)]
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = []
+    for x, st in ((xa, s1), (xb, s2), (xa, s2), (xb, s1)):
+        with torch.cuda.stream(st):
+            a = torch.from_numpy(x).cuda(non_blocking=False)
+            idx = torch.empty(rows, dtype=torch.int32, device="cuda")
+            prob = torch.empty(rows, dtype=torch.float32, device="cuda")
+        st.synchronize()  # inputs in place; the head calls below are not synchronised
+        rh.head_decode_device(qw, a.data_ptr(), rows, idx.data_ptr(), prob.data_ptr(), st.cuda_stream)
+        outs.append((a, idx, prob))
+    torch.cuda.synchronize()
+    ctx.sync()
+    for i, (_, idx, prob) in enumerate(outs):
+        r_idx, r_prob = ref[i % 2]
+        assert np.array_equal(idx.cpu().numpy(), r_idx), i
+        assert np.array_equal(prob.cpu().numpy().view(np.uint32), r_prob.view(np.uint32)), i
+    qw.free()
+
+
 def test_bounded_wait_reports_timeout_and_context_survives(rh, oracle, monkeypatch):
     """Failure detection without a GPU fault: the weight producer is told (test flag) never
     to fill its stages, so the consumers' bounded waits run out after 200 ms; the kernel
