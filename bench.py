@@ -179,6 +179,17 @@ def measured_peak_tflops():
         return 1590.0, "fallback 1.59 PFLOP/s bf16 dense"
 
 
+def output_checksum(*tensors):
+    """CRC32 of the raw bytes of the last step's device outputs (same work, same bytes: equal
+    across runs and across the kernel's versions, whatever the timing)."""
+    import zlib
+
+    crc = 0
+    for t in tensors:
+        crc = zlib.crc32(t.detach().cpu().contiguous().numpy().tobytes(), crc)
+    return f"crc32:{crc:08x}"
+
+
 def measured_hbm_gbs():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -403,6 +414,7 @@ def run_recpre(args, world, rank, local, torch, rh, barrier, max_over_ranks):
                      "note": "achieved = (crop bytes + output bytes) per step / device time per step (tap-table "
                              "kernel + resize kernel + descriptor copy)"},
         "clocks": clocks.summary(),
+        "checksum": output_checksum(d_out),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, threads, ns, reps, dt = cpu_recpre(blob, offsets, widths, heights, min(args.cpu_sample_lines, 256))
@@ -548,6 +560,7 @@ def main():
         "gpu_launches": int(launches),
         "roofline": roofline,
         "clocks": clocks.summary(),
+        "checksum": output_checksum(idx, prob),
     }
     if args.weights == "f32":
         out["config"]["weights"] = "f32 (hi/lo fp16 images, 23 MMA K-steps per tile)"

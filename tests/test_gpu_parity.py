@@ -514,9 +514,10 @@ def test_device_pointer_entry_points_match_host(rh, ctx):
     idx_h, prob_h = rh.head_decode(wl.x, qw)
     logits_h = rh.matmul_quantized_b(wl.x[:50], qw, wl.bias)
     a = torch.from_numpy(wl.x).cuda()
-    idx = torch.empty(wl.rows, dtype=torch.int32, device="cuda")
-    prob = torch.empty(wl.rows, dtype=torch.float32, device="cuda")
-    out = torch.empty((50, qw.rows), dtype=torch.float32, device="cuda")
+    # poisoned outputs: every element must be written
+    idx = torch.full((wl.rows,), -1, dtype=torch.int32, device="cuda")
+    prob = torch.full((wl.rows,), float("nan"), dtype=torch.float32, device="cuda")
+    out = torch.full((50, qw.rows), float("nan"), dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
     rh.head_decode_device(qw, a.data_ptr(), wl.rows, idx.data_ptr(), prob.data_ptr(), stream)
     rh.matmul_quantized_b_device(qw, a.data_ptr(), 50, out.data_ptr(), stream)
