@@ -528,6 +528,36 @@ def test_device_pointer_entry_points_match_host(rh, ctx):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), logits_h.view(np.uint32))
 
 
+def test_non_finite_features_stay_in_their_rows(rh, ctx, oracle):
+    """Rows with NaN / Inf features (garbage in) sit beside finite rows: the finite rows keep
+    exact parity with the oracle, and every row gets a class index in range. The non-finite
+    rows themselves are outside the parity bar: the reference's result for them depends on
+    which AVX2 lanes hold the NaN / Inf (one NaN logit at class 0 leaves the argmax and a
+    finite probability, one +Inf at class 7000 gives (0, 5.3e-5), all-NaN gives
+    (0, 1.18e-38)); here such a row's probability is not finite."""
+    from rust_ppocrv6_b200 import workloads
+
+    wl = workloads.make(0)
+    qw = rh.QuantizedWeight.from_f32_transposed(wl.w_t, ctx=ctx, bias=wl.bias)
+    x = wl.x[:64].copy()
+    bad = [1, 2, 3, 4, 5, 40]
+    x[1, 5] = np.nan
+    x[2, 7] = np.inf
+    x[3, 9] = -np.inf
+    x[4, :] = np.nan
+    x[5, 3] = 3e38
+    x[40, 0] = np.nan
+    idx, prob = rh.head_decode(x, qw)
+    q, s = oracle.pack(wl.w_t)
+    ref = oracle.head_decode(x, np.array([0, 64], np.int64), q, s, wl.bias, threads=4, want_gap=True)
+    good = np.setdiff1d(np.arange(64), bad)
+    sub = {k: v[good] for k, v in ref.items() if hasattr(v, "shape") and v.shape[:1] == (64,)}
+    assert_fused(idx[good], prob[good], sub, "finite rows beside non-finite ones")
+    assert np.all((idx >= 0) & (idx < wl.w_t.shape[0]))
+    print("non-finite rows:", list(zip(idx[bad].tolist(), prob[bad].tolist())))
+    qw.free()
+
+
 def test_device_calls_on_two_streams_share_the_slot_safely(rh, ctx):
     """Two device-form calls on one slot from different caller streams, back to back with no
     synchronisation: both use the slot's split scratch (few rows -> the class range is split),
