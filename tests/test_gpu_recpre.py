@@ -213,3 +213,15 @@ def test_concurrent_callers_share_a_context(rh, ctx, oracle):
     for i, (got, _) in enumerate(results):
         ref, _ = oracle.rec_preprocess_batch(batches[i])
         assert_same(got, ref, f"thread {i}")
+
+
+def test_wide_lines_staged_in_several_chunks(rh, ctx, oracle):
+    """max_w = 4000: lines wider than one 2,048-column stage are resized in chunks of output
+    columns, through the horizontal pass that reads its windows from the tables (kx = 2 and
+    3); a narrow line in the same batch still stages its windows once per block."""
+    dims = [(3000, 30), (1500, 20), (2900, 64), (100, 40), (4000, 10)]
+    crops = crops_of(dims, 23)
+    got, widths = rh.RecPreprocess(48, 4000, ctx=ctx).process_batch(crops)
+    assert list(widths) == [4000, 3600, 2175, 120, 4000]
+    ref, _ = oracle.rec_preprocess_batch(crops, 48, 4000, threads=4)
+    assert_same(got, ref, "wide lines")
