@@ -541,7 +541,7 @@ def main():
     traffic = profiled_traffic()
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "peak_source": peak_src,
-                "traffic": traffic if args.workload == "cfg2" else None,
+                "traffic": traffic if args.workload == "cfg2" and args.weights == "int8" else None,
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one cfg2 launch "
                                   "(profiles/head_kernel_cfg2_ncu_full.md)",
                 "tf32_equiv_frac": achieved / (peak / 2),
