@@ -235,6 +235,19 @@ int rh_ctc_collapse_device(rh_ctx *ctx, int slot, const int32_t *d_idx, const fl
 int rh_head_decode_ctc(rh_ctx *ctx, const rh_weight *w, const float *a, const int64_t *line_offsets, int64_t n_lines,
                        int64_t k, int32_t *tokens, int64_t *token_offsets, float *scores);
 
+/*
+ * A padded batch end to end: the SVTR tail's [batch][k][t_len] output of a batch whose lines
+ * were padded to one width (the packing of tools/profiling/batch_poc.rs:14-32), line b valid
+ * for its first valid_t[b] timesteps (0 <= valid_t[b] <= t_len). The head runs on every
+ * timestep as rh_head_decode_kt does (Transpose.8 folded into the loads), then the CTC collapse
+ * of rh_ctc_collapse runs on the GPU over each line's valid timesteps only, which is what the
+ * per-line chain of OcrEngine::recognize (src/pipeline.rs:364-436) decodes for that line.
+ * Outputs as rh_ctc_collapse: tokens (room for sum(valid_t) entries), token_offsets
+ * [batch + 1], scores [batch]; host memory, first context device.
+ */
+int rh_head_decode_kt_ctc(rh_ctx *ctx, const rh_weight *w, const float *x, int64_t batch, int64_t k, int64_t t_len,
+                          const int64_t *valid_t, int32_t *tokens, int64_t *token_offsets, float *scores);
+
 /* ------------------------------------------------ batched recognition preprocessing
  *
  * The producer side of the head: text-line crops (RGB8, row-major HWC, 3 bytes per pixel)

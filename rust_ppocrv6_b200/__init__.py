@@ -11,12 +11,14 @@ from ._lib import (RH_ERR_CUDA, RH_ERR_DEVICE_FAULT, RH_ERR_INVALID_ARG, RH_ERR_
 from .ctc import CtcDecoder
 from .preprocess import RecPreprocess, batch_shape, rec_preprocess_device, resized_width
 from .head import (Context, Fp32Weight, QuantizedWeight, ctc_collapse_device, default_context, head_decode,
-                   head_decode_ctc, head_decode_device, head_decode_kt, matmul_quantized_b, matmul_quantized_b_device,
+                   head_decode_ctc, head_decode_device, head_decode_kt, head_decode_kt_ctc, matmul_quantized_b,
+                   matmul_quantized_b_device,
                    matmul_transposed_b)
 
 __all__ = [
     "Context", "QuantizedWeight", "Fp32Weight", "CtcDecoder", "RecHeadError",
-    "matmul_quantized_b", "matmul_transposed_b", "head_decode", "head_decode_kt", "head_decode_ctc",
+    "matmul_quantized_b", "matmul_transposed_b", "head_decode", "head_decode_kt", "head_decode_kt_ctc",
+    "head_decode_ctc",
     "head_decode_device", "matmul_quantized_b_device", "ctc_collapse_device",
     "default_context", "load", "header_symbols",
     "RecPreprocess", "resized_width", "batch_shape", "rec_preprocess_device",

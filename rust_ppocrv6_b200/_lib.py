@@ -56,6 +56,7 @@ SIGNATURES = {
     "rh_ctc_collapse": (_c_i64, [_vp, _vp, _vp, _c_i64, _vp, _vp, _vp]),
     "rh_ctc_collapse_device": (_c_int, [_vp, _c_int, _vp, _vp, _vp, _c_i64, _vp, _vp, _vp, _vp]),
     "rh_head_decode_ctc": (_c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _vp, _vp, _vp]),
+    "rh_head_decode_kt_ctc": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _vp]),
     "rh_rec_resized_width": (_u32, [_u32, _u32, _u32, _u32]),
     "rh_rec_batch_shape": (_c_int, [_vp, _vp, _c_i64, _u32, _u32, _vp, _vp, _vp]),
     "rh_rec_preprocess": (_c_int, [_vp, _vp, _c_i64, _vp, _vp, _vp, _c_i64, _u32, _u32, _vp, _c_i64, _vp, _vp]),

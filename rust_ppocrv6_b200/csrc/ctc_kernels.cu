@@ -24,9 +24,12 @@ namespace {
 
 constexpr int kCtcThreads = 256;  // 8 lines per block
 
-__device__ __forceinline__ void line_range(const int64_t* __restrict__ offs, int64_t l, int64_t& b, int64_t& e) {
+// Line l owns timesteps [offs[l], offs[l + 1]), or [offs[l], ends[l]) when the lines have gaps
+// between them (padded batches: ends given).
+__device__ __forceinline__ void line_range(const int64_t* __restrict__ offs, const int64_t* __restrict__ ends,
+                                           int64_t l, int64_t& b, int64_t& e) {
     b = offs[l];
-    e = offs[l + 1];
+    e = ends ? ends[l] : offs[l + 1];
     if (e < b) e = b;  // a decreasing pair is treated as an empty line (host entry points reject it)
 }
 
@@ -42,13 +45,14 @@ __device__ __forceinline__ bool emits(const int32_t* __restrict__ idx, int64_t t
 }  // namespace
 
 __global__ void __launch_bounds__(kCtcThreads) ctc_count_kernel(const int32_t* __restrict__ idx,
-                                                                 const int64_t* __restrict__ offs, int64_t n_lines,
+                                                                 const int64_t* __restrict__ offs,
+                                                                 const int64_t* __restrict__ ends, int64_t n_lines,
                                                                  int64_t* __restrict__ token_offsets) {
     const int64_t l = ((int64_t)blockIdx.x * kCtcThreads + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (l >= n_lines) return;
     int64_t b, e;
-    line_range(offs, l, b, e);
+    line_range(offs, ends, l, b, e);
     int64_t count = 0;
     for (int64_t t0 = b; t0 < e; t0 += 32) {
         int32_t c;
@@ -97,7 +101,8 @@ __global__ void __launch_bounds__(1024) ctc_scan_kernel(int64_t* __restrict__ to
 
 __global__ void __launch_bounds__(kCtcThreads) ctc_emit_kernel(const int32_t* __restrict__ idx,
                                                                 const float* __restrict__ prob,
-                                                                const int64_t* __restrict__ offs, int64_t n_lines,
+                                                                const int64_t* __restrict__ offs,
+                                                                const int64_t* __restrict__ ends, int64_t n_lines,
                                                                 const int64_t* __restrict__ token_offsets,
                                                                 int32_t* __restrict__ tokens,
                                                                 float* __restrict__ scores) {
@@ -105,7 +110,7 @@ __global__ void __launch_bounds__(kCtcThreads) ctc_emit_kernel(const int32_t* __
     const int lane = threadIdx.x & 31;
     if (l >= n_lines) return;
     int64_t b, e;
-    line_range(offs, l, b, e);
+    line_range(offs, ends, l, b, e);
     int64_t pos = token_offsets[l];
     float sum = 0.0f;
     int64_t count = 0;
@@ -124,14 +129,16 @@ __global__ void __launch_bounds__(kCtcThreads) ctc_emit_kernel(const int32_t* __
 }
 
 cudaError_t launch_ctc_collapse(const int32_t* idx, const float* prob, const int64_t* line_offsets, int64_t n_lines,
-                                int32_t* tokens, int64_t* token_offsets, float* scores, cudaStream_t stream) {
+                                int32_t* tokens, int64_t* token_offsets, float* scores, cudaStream_t stream,
+                                const int64_t* line_ends) {
     const int64_t blocks = (n_lines * 32 + kCtcThreads - 1) / kCtcThreads;
-    if (n_lines > 0) ctc_count_kernel<<<(unsigned)blocks, kCtcThreads, 0, stream>>>(idx, line_offsets, n_lines,
-                                                                                    token_offsets);
+    if (n_lines > 0)
+        ctc_count_kernel<<<(unsigned)blocks, kCtcThreads, 0, stream>>>(idx, line_offsets, line_ends, n_lines,
+                                                                       token_offsets);
     ctc_scan_kernel<<<1, 1024, 0, stream>>>(token_offsets, n_lines);
     if (n_lines > 0)
-        ctc_emit_kernel<<<(unsigned)blocks, kCtcThreads, 0, stream>>>(idx, prob, line_offsets, n_lines, token_offsets,
-                                                                      tokens, scores);
+        ctc_emit_kernel<<<(unsigned)blocks, kCtcThreads, 0, stream>>>(idx, prob, line_offsets, line_ends, n_lines,
+                                                                      token_offsets, tokens, scores);
     return cudaGetLastError();
 }
 

@@ -113,9 +113,11 @@ cudaError_t launch_pack(const PackParams& p, cudaStream_t stream);
 cudaError_t launch_head(const HeadParams& p, bool emit_logits, int grid, cudaStream_t stream);
 cudaError_t launch_merge(const float4* partial, int n_splits, long long m, int32_t* idx, float* prob,
                          cudaStream_t stream);
-// CTC greedy collapse of per-timestep (idx, prob) in device memory (ctc_kernels.cu).
+// CTC greedy collapse of per-timestep (idx, prob) in device memory (ctc_kernels.cu). Line l is
+// [line_offsets[l], line_offsets[l + 1]), or [line_offsets[l], line_ends[l]) when line_ends is given.
 cudaError_t launch_ctc_collapse(const int32_t* idx, const float* prob, const int64_t* line_offsets, int64_t n_lines,
-                                int32_t* tokens, int64_t* token_offsets, float* scores, cudaStream_t stream);
+                                int32_t* tokens, int64_t* token_offsets, float* scores, cudaStream_t stream,
+                                const int64_t* line_ends = nullptr);
 // Tap windows and weights of every line (one launch), then the resize of lines [line0, line0 + n).
 cudaError_t launch_rec_weights(const RecParams& p, cudaStream_t stream);
 cudaError_t launch_rec_resize(const RecParams& p, long long line0, long long n, cudaStream_t stream);

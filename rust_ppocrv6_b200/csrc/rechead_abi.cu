@@ -991,6 +991,75 @@ int rh_head_decode_kt(rh_ctx* ctx, const rh_weight* w, const float* x, int64_t b
     return read_status(s);
 }
 
+int rh_head_decode_kt_ctc(rh_ctx* ctx, const rh_weight* w, const float* x, int64_t batch, int64_t k, int64_t t_len,
+                          const int64_t* valid_t, int32_t* tokens, int64_t* token_offsets, float* scores) {
+    if (int rc = check_ctx(ctx)) return rc;
+    if (!w) return fail(RH_ERR_INVALID_ARG, "null weight");
+    if (k != w->k)
+        return fail(RH_ERR_INVALID_ARG,
+                    "Inner dimensions must match: " + std::to_string(k) + " != " + std::to_string(w->k));
+    if (batch < 0 || t_len < 0) return fail(RH_ERR_INVALID_ARG, "negative batch or sequence length");
+    if (!token_offsets) return fail(RH_ERR_INVALID_ARG, "null token offsets");
+    token_offsets[0] = 0;
+    if (batch == 0) return RH_OK;
+    if (!valid_t || !scores) return fail(RH_ERR_INVALID_ARG, "null valid lengths or scores");
+    std::vector<int64_t> ranges(2 * (size_t)batch);  // line starts, then line ends (rows of the batch)
+    int64_t total = 0;
+    for (int64_t b = 0; b < batch; ++b) {
+        if (valid_t[b] < 0 || valid_t[b] > t_len)
+            return fail(RH_ERR_INVALID_ARG, "valid length " + std::to_string(valid_t[b]) + " of line " +
+                                                std::to_string(b) + " is outside [0, " + std::to_string(t_len) + "]");
+        ranges[b] = b * t_len;
+        ranges[batch + b] = b * t_len + valid_t[b];
+        total += valid_t[b];
+    }
+    if (total == 0) {  // every line empty: no tokens, score 0
+        for (int64_t b = 0; b < batch; ++b) {
+            token_offsets[b + 1] = 0;
+            scores[b] = 0.0f;
+        }
+        return RH_OK;
+    }
+    if (!x || !tokens) return fail(RH_ERR_INVALID_ARG, "null input or tokens");
+    const int64_t rows = batch * t_len;
+    Slot& s = *ctx->slots[0];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
+    const size_t x_bytes = (size_t)rows * (size_t)k * sizeof(float);
+    RH_CUDA(s.a.ensure(x_bytes));
+    RH_CUDA(s.idx.ensure((size_t)rows * sizeof(int32_t)));
+    RH_CUDA(s.prob.ensure((size_t)rows * sizeof(float)));
+    RH_CUDA(s.lines.ensure(ranges.size() * sizeof(int64_t)));
+    RH_CUDA(s.tok_off.ensure((size_t)(batch + 1) * sizeof(int64_t)));
+    RH_CUDA(s.tokens.ensure((size_t)total * sizeof(int32_t)));
+    RH_CUDA(s.scores.ensure((size_t)batch * sizeof(float)));
+    RH_CUDA(cudaMemcpyAsync(s.a.p, x, x_bytes, cudaMemcpyHostToDevice, s.stream));
+    if (int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, (int32_t*)s.idx.p, (float*)s.prob.p, nullptr,
+                              false, s.stream, t_len))
+        return rc;
+    RH_CUDA(cudaMemcpyAsync(s.lines.p, ranges.data(), ranges.size() * sizeof(int64_t), cudaMemcpyHostToDevice,
+                            s.stream));
+    const int64_t* d_begin = (const int64_t*)s.lines.p;
+    RH_CUDA(rh::launch_ctc_collapse((const int32_t*)s.idx.p, (const float*)s.prob.p, d_begin, batch,
+                                    (int32_t*)s.tokens.p, (int64_t*)s.tok_off.p, (float*)s.scores.p, s.stream,
+                                    d_begin + batch));
+    s.launches += 3;
+    RH_CUDA(cudaMemcpyAsync(token_offsets, s.tok_off.p, (size_t)(batch + 1) * sizeof(int64_t), cudaMemcpyDeviceToHost,
+                            s.stream));
+    RH_CUDA(cudaMemcpyAsync(scores, s.scores.p, (size_t)batch * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    if (int rc = read_status(s)) return rc;
+    const int64_t n_tok = token_offsets[batch];
+    if (n_tok < 0 || n_tok > total) return fail(RH_ERR_CUDA, "CTC collapse produced an impossible token count");
+    if (n_tok > 0) {
+        RH_CUDA(cudaMemcpyAsync(tokens, s.tokens.p, (size_t)n_tok * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
+        RH_CUDA(cudaStreamSynchronize(s.stream));
+    }
+    return RH_OK;
+}
+
 int rh_head_decode_device(rh_ctx* ctx, const rh_weight* w, int slot, const float* d_a, int64_t rows, int32_t* d_idx,
                           float* d_prob, void* stream) {
     if (int rc = check_ctx(ctx)) return rc;

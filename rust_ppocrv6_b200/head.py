@@ -287,6 +287,28 @@ def head_decode_kt(x, qw: QuantizedWeight, bias=None):
     return idx, prob
 
 
+def head_decode_kt_ctc(x, qw: QuantizedWeight, valid_t, bias=None):
+    """A padded batch end to end (rh_head_decode_kt_ctc): the SVTR tail's [batch, k, T] output,
+    line b valid for its first valid_t[b] timesteps; the head on the GPU, then the CTC collapse
+    over each line's valid timesteps. Returns (tokens, token_offsets, scores) as
+    rh_ctc_collapse."""
+    x = _f32(x)
+    if x.ndim != 3 or x.shape[1] != qw.cols:
+        raise RecHeadError(RH_ERR_INVALID_ARG, f"expected [batch, {qw.cols}, T] features, got {x.shape}")
+    if bias is not None:
+        _use_bias(qw, bias)
+    b, k, t = x.shape
+    vt = np.ascontiguousarray(valid_t, dtype=np.int64)
+    if vt.shape != (b,):
+        raise RecHeadError(RH_ERR_INVALID_ARG, f"valid_t must hold one length per line ({b}), got {vt.shape}")
+    tokens = np.empty(max(int(vt.sum()) if b else 0, 1), np.int32)
+    toff = np.zeros(b + 1, np.int64)
+    scores = np.empty(max(b, 1), np.float32)
+    check(load().rh_head_decode_kt_ctc(qw._ctx.handle, qw.handle, _p(x), b, k, t, _p(vt) if b else None, _p(tokens),
+                                       _p(toff), _p(scores)))
+    return tokens[:toff[-1]].copy(), toff, scores[:b].copy()
+
+
 def head_decode_ctc(a, qw: QuantizedWeight, line_offsets, bias=None):
     """The head of a line batch with the CTC collapse on the GPU (rh_head_decode_ctc):
     returns (tokens int32 [total], token_offsets int64 [n_lines + 1], scores f32 [n_lines]),

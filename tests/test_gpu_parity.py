@@ -528,6 +528,43 @@ def test_device_pointer_entry_points_match_host(rh, ctx):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), logits_h.view(np.uint32))
 
 
+def test_padded_batch_decodes_each_line_over_its_valid_timesteps(rh, ctx, oracle):
+    """rh_head_decode_kt_ctc on a [batch, K, T] batch padded to one width: each line's tokens and
+    score are those of its first valid_t[b] timesteps only (bit-identical to the host collapse
+    of rh_head_decode_kt's per-timestep output over the valid rows), and the per-timestep
+    decode of the valid rows has parity with the oracle."""
+    from rust_ppocrv6_b200 import workloads
+
+    wl = workloads.make(0)
+    qw = rh.QuantizedWeight.from_f32_transposed(wl.w_t, ctx=ctx, bias=wl.bias)
+    rng = np.random.default_rng(71)
+    B, T = 14, 40
+    x = rng.standard_normal((B, wl.w_t.shape[1], T), dtype=np.float32)
+    valid = np.array([T, 0, 1, 17, T, 5, 39, 2, 0, 23, T, 8, 31, 12], np.int64)
+    tokens, toff, scores = rh.head_decode_kt_ctc(x, qw, valid)
+    idx, prob = rh.head_decode_kt(x, qw)
+    iv = np.concatenate([idx[b, :valid[b]] for b in range(B)])
+    pv = np.concatenate([prob[b, :valid[b]] for b in range(B)])
+    off = np.concatenate([[0], np.cumsum(valid)]).astype(np.int64)
+    ht, hs = rh.CtcDecoder([]).collapse(iv, pv, off)
+    assert np.array_equal(toff, np.concatenate([[0], np.cumsum([t.size for t in ht])]))
+    assert np.array_equal(tokens, np.concatenate(ht) if len(ht) else np.zeros(0, np.int32))
+    assert np.array_equal(scores.view(np.uint32), np.asarray(hs, np.float32).view(np.uint32))
+    assert np.all(scores[valid == 0] == 0.0) and np.all(np.diff(toff)[valid == 0] == 0)
+    rows = np.ascontiguousarray(np.concatenate([x[b, :, :valid[b]].T for b in range(B)]))
+    q, s = oracle.pack(wl.w_t)
+    ref = oracle.head_decode(rows, off, q, s, wl.bias, threads=4, want_gap=True)
+    assert_fused(iv, pv, ref, "padded batch")
+    # every line empty, and an empty batch
+    t0, o0, s0 = rh.head_decode_kt_ctc(x, qw, np.zeros(B, np.int64))
+    assert t0.size == 0 and np.all(o0 == 0) and np.all(s0 == 0.0)
+    t1, o1, s1 = rh.head_decode_kt_ctc(x[:0], qw, np.zeros(0, np.int64))
+    assert t1.size == 0 and o1.tolist() == [0] and s1.size == 0
+    with pytest.raises(rh.RecHeadError):
+        rh.head_decode_kt_ctc(x, qw, np.full(B, T + 1, np.int64))
+    qw.free()
+
+
 def test_non_finite_features_stay_in_their_rows(rh, ctx, oracle):
     """Rows with NaN / Inf features (garbage in) sit beside finite rows: the finite rows keep
     exact parity with the oracle, and every row gets a class index in range. The non-finite
