@@ -225,3 +225,38 @@ def test_wide_lines_staged_in_several_chunks(rh, ctx, oracle):
     assert list(widths) == [4000, 3600, 2175, 120, 4000]
     ref, _ = oracle.rec_preprocess_batch(crops, 48, 4000, threads=4)
     assert_same(got, ref, "wide lines")
+
+
+def _random_batches(seed=31, n_batches=24):
+    """Seeded batches of crops of every shape class: text lines, tall/narrow, wide/flat, tiny
+    or empty; random target heights and width caps."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n_batches):
+        n = int(rng.integers(1, 9))
+        th = int(rng.choice([1, 16, 32, 48, 64]))
+        mw = int(rng.choice([8, 100, 320, 960, 2000, 4000]))
+        dims = []
+        for _ in range(n):
+            kind = rng.integers(0, 4)
+            if kind == 0:
+                h = int(rng.integers(8, 100))
+                w = int(h * rng.uniform(2, 30))
+            elif kind == 1:
+                w, h = int(rng.integers(1, 40)), int(rng.integers(40, 600))
+            elif kind == 2:
+                h, w = int(rng.integers(1, 12)), int(rng.integers(100, 9000))
+            else:
+                w, h = int(rng.integers(0, 6)), int(rng.integers(0, 6))
+            dims.append((w, h))
+        out.append((dims, th, mw))
+    return out
+
+
+def test_randomized_batches_bit_exact(rh, ctx, oracle):
+    for i, (dims, th, mw) in enumerate(_random_batches()):
+        crops = crops_of(dims, 100 + i)
+        got, widths = rh.RecPreprocess(th, mw, ctx=ctx).process_batch(crops)
+        ref, ref_w = oracle.rec_preprocess_batch(crops, th, mw, threads=8)
+        assert np.array_equal(widths, ref_w), (i, dims, th, mw)
+        assert_same(got, ref, f"batch {i}: {dims} H={th} max_w={mw}")
