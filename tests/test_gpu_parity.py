@@ -565,6 +565,25 @@ def test_padded_batch_decodes_each_line_over_its_valid_timesteps(rh, ctx, oracle
     qw.free()
 
 
+def test_randomized_shapes_against_oracle(rh, ctx, oracle):
+    """Seeded random heads and batches (M, N, K within the supported range, bias or not):
+    packed weights bit-exact, logits within the bar, fused argmax/prob within the bars."""
+    rng = np.random.default_rng(97)
+    for i in range(16):
+        m, n, k = int(rng.integers(1, 700)), int(rng.integers(1, 3000)), int(rng.integers(1, 129))
+        w = (0.05 * rng.standard_normal((n, k))).astype(np.float32)
+        bias = (0.01 * rng.standard_normal(n)).astype(np.float32) if rng.random() < 0.7 else None
+        a = rng.standard_normal((m, k), dtype=np.float32)
+        qw, q, s = pack_both(rh, ctx, oracle, w, bias)
+        assert np.array_equal(qw.data, q) and np.array_equal(qw.scales.view(np.uint32), s.view(np.uint32))
+        ref = oracle.head_decode(a, np.array([0, m], np.int64), q, s, bias, threads=8, want_logits=True,
+                                 want_gap=True)
+        assert_logits_close(rh.matmul_quantized_b(a, qw, bias), ref["logits"])
+        idx, prob = rh.head_decode(a, qw, bias)
+        assert_fused(idx, prob, ref, f"random {i}: m={m} n={n} k={k}")
+        qw.free()
+
+
 def test_non_finite_features_stay_in_their_rows(rh, ctx, oracle):
     """Rows with NaN / Inf features (garbage in) sit beside finite rows: the finite rows keep
     exact parity with the oracle, and every row gets a class index in range. The non-finite
