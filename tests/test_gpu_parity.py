@@ -582,6 +582,16 @@ def test_randomized_shapes_against_oracle(rh, ctx, oracle):
         idx, prob = rh.head_decode(a, qw, bias)
         assert_fused(idx, prob, ref, f"random {i}: m={m} n={n} k={k}")
         qw.free()
+        # the same shape through the FP32 head (the engine's default)
+        fw = rh.Fp32Weight.from_f32_transposed(w, ctx=ctx, bias=bias)
+        logits32, ref32 = _oracle_f32_head(oracle, a, w, bias)
+        got32 = rh.matmul_transposed_b(a, fw, bias)
+        terms = np.abs(a).astype(np.float64) @ np.abs(w).astype(np.float64).T
+        err = np.abs(got32.astype(np.float64) - logits32)
+        assert np.all(err <= LOGIT_ABS_TOL + LOGIT_REL_TOL * terms), f"fp32 random {i}: max err {err.max():.3g}"
+        idx32, prob32 = rh.head_decode(a, fw, bias)
+        assert_fused(idx32, prob32, ref32, f"fp32 random {i}: m={m} n={n} k={k}")
+        fw.free()
 
 
 def test_non_finite_features_stay_in_their_rows(rh, ctx, oracle):
