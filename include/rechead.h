@@ -147,8 +147,9 @@ int rh_head_decode_lines(rh_ctx *ctx, const rh_weight *w, const float *a, const 
  * Squeeze.7/Transpose.8), so the transpose to [batch*t_len][k] rows that feeds MatMul.12 is
  * folded into the kernel's feature loads (each converter thread gathers its timestep row; a
  * warp reads 32 consecutive timesteps per feature, coalesced). idx/prob are [batch*t_len] in
- * (b, t) order, exactly what rh_head_decode returns for the transposed rows. Host memory, first
- * device; the _device form takes device pointers and a stream.
+ * (b, t) order, exactly what rh_head_decode returns for the transposed rows. Host memory, the
+ * batch split into equal line shards over the context's devices (as rh_head_decode_lines);
+ * the _device form takes device pointers and a stream.
  */
 int rh_head_decode_kt(rh_ctx *ctx, const rh_weight *w, const float *x, int64_t batch, int64_t k, int64_t t_len,
                       int32_t *idx, float *prob);
@@ -243,7 +244,8 @@ int rh_head_decode_ctc(rh_ctx *ctx, const rh_weight *w, const float *a, const in
  * of rh_ctc_collapse runs on the GPU over each line's valid timesteps only, which is what the
  * per-line chain of OcrEngine::recognize (src/pipeline.rs:364-436) decodes for that line.
  * Outputs as rh_ctc_collapse: tokens (room for sum(valid_t) entries), token_offsets
- * [batch + 1], scores [batch]; host memory, first context device.
+ * [batch + 1], scores [batch]; host memory, the batch split into equal line shards over the
+ * context's devices (as rh_head_decode_ctc).
  */
 int rh_head_decode_kt_ctc(rh_ctx *ctx, const rh_weight *w, const float *x, int64_t batch, int64_t k, int64_t t_len,
                           const int64_t *valid_t, int32_t *tokens, int64_t *token_offsets, float *scores);

@@ -419,6 +419,129 @@ int noalloc_scratch(int device, float4** out) {
     return RH_OK;
 }
 
+// ------------------------------------------------------------- sharded batches
+// Runs job(d, slot) for the shards d = 0..nd-1 (shard d on slot d, one host thread per device
+// when nd > 1), then redoes every failed shard on a healthy device (results do not depend on
+// the device); an invalid-argument failure is returned as it is. Host-side failure injection:
+// RH_FAULT_DEVICE=<slot>[,<slot>...] makes those slots fail their shards.
+template <class Job>
+int run_shards(int nd, Job&& job) {
+    const std::vector<int> faults = injected_fault_slots();
+    std::vector<int> rc(nd, RH_OK);
+    std::vector<std::string> msg(nd);
+    auto run = [&](int d, int on_slot) {
+        if (std::find(faults.begin(), faults.end(), on_slot) != faults.end()) {
+            rc[d] = RH_ERR_DEVICE_FAULT;
+            msg[d] = "injected failure on slot " + std::to_string(on_slot);
+            return;
+        }
+        rc[d] = job(d, on_slot);
+        if (rc[d]) msg[d] = g_err;
+    };
+    if (nd == 1) {
+        run(0, 0);
+    } else {
+        std::vector<std::thread> th;
+        for (int d = 0; d < nd; ++d) th.emplace_back(run, d, d);
+        for (auto& t : th) t.join();
+    }
+    int healthy = -1;
+    for (int d = 0; d < nd; ++d)
+        if (rc[d] == RH_OK && std::find(faults.begin(), faults.end(), d) == faults.end()) {
+            healthy = d;
+            break;
+        }
+    for (int d = 0; d < nd; ++d) {
+        if (rc[d] == RH_OK) continue;
+        if (rc[d] == RH_ERR_INVALID_ARG) return fail(rc[d], msg[d]);
+        if (healthy < 0) return fail(RH_ERR_DEVICE_FAULT, "every device shard failed; last: " + msg[d]);
+        run(d, healthy);
+        if (rc[d] != RH_OK) return fail(rc[d], msg[d]);
+    }
+    return RH_OK;
+}
+
+// The head on `nb` lines of the SVTR tail's [nb][k][t_len] output on one slot (host memory).
+int kt_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* x, int64_t nb, int64_t t_len, int32_t* idx,
+               float* prob) {
+    const int64_t rows = nb * t_len;
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
+    const size_t x_bytes = (size_t)rows * (size_t)w->k * sizeof(float);
+    RH_CUDA(s.a.ensure(x_bytes));
+    RH_CUDA(s.idx.ensure((size_t)rows * sizeof(int32_t)));
+    RH_CUDA(s.prob.ensure((size_t)rows * sizeof(float)));
+    RH_CUDA(cudaMemcpyAsync(s.a.p, x, x_bytes, cudaMemcpyHostToDevice, s.stream));
+    if (int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, (int32_t*)s.idx.p, (float*)s.prob.p, nullptr,
+                              false, s.stream, t_len))
+        return rc;
+    RH_CUDA(cudaMemcpyAsync(idx, s.idx.p, (size_t)rows * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaMemcpyAsync(prob, s.prob.p, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    return read_status(s);
+}
+
+// The head and the GPU collapse of `nb` padded lines (line b valid for valid_t[b] <= t_len
+// timesteps) on one slot: tokens (room for the shard's valid rows), token_offsets [nb + 1]
+// from 0 and scores [nb] in host memory.
+int kt_ctc_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* x, int64_t nb, int64_t t_len,
+                   const int64_t* valid_t, int32_t* tokens, int64_t* token_offsets, float* scores) {
+    std::vector<int64_t> ranges(2 * (size_t)nb);  // line starts, then line ends (rows of the shard)
+    int64_t total = 0;
+    for (int64_t b = 0; b < nb; ++b) {
+        ranges[b] = b * t_len;
+        ranges[nb + b] = b * t_len + valid_t[b];
+        total += valid_t[b];
+    }
+    token_offsets[0] = 0;
+    if (total == 0) {  // every line empty: no tokens, score 0
+        for (int64_t b = 0; b < nb; ++b) {
+            token_offsets[b + 1] = 0;
+            scores[b] = 0.0f;
+        }
+        return RH_OK;
+    }
+    const int64_t rows = nb * t_len;
+    Slot& s = *ctx->slots[slot];
+    std::lock_guard<std::mutex> lock(s.mu);
+    RH_CUDA(cudaSetDevice(s.device));
+    const rh_weight::Per* pw = weight_on(w, s.device);
+    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
+    const size_t x_bytes = (size_t)rows * (size_t)w->k * sizeof(float);
+    RH_CUDA(s.a.ensure(x_bytes));
+    RH_CUDA(s.idx.ensure((size_t)rows * sizeof(int32_t)));
+    RH_CUDA(s.prob.ensure((size_t)rows * sizeof(float)));
+    RH_CUDA(s.lines.ensure(ranges.size() * sizeof(int64_t)));
+    RH_CUDA(s.tok_off.ensure((size_t)(nb + 1) * sizeof(int64_t)));
+    RH_CUDA(s.tokens.ensure((size_t)total * sizeof(int32_t)));
+    RH_CUDA(s.scores.ensure((size_t)nb * sizeof(float)));
+    RH_CUDA(cudaMemcpyAsync(s.a.p, x, x_bytes, cudaMemcpyHostToDevice, s.stream));
+    if (int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, (int32_t*)s.idx.p, (float*)s.prob.p, nullptr,
+                              false, s.stream, t_len))
+        return rc;
+    RH_CUDA(cudaMemcpyAsync(s.lines.p, ranges.data(), ranges.size() * sizeof(int64_t), cudaMemcpyHostToDevice,
+                            s.stream));
+    const int64_t* d_begin = (const int64_t*)s.lines.p;
+    RH_CUDA(rh::launch_ctc_collapse((const int32_t*)s.idx.p, (const float*)s.prob.p, d_begin, nb, (int32_t*)s.tokens.p,
+                                    (int64_t*)s.tok_off.p, (float*)s.scores.p, s.stream, d_begin + nb));
+    s.launches += 3;
+    RH_CUDA(cudaMemcpyAsync(token_offsets, s.tok_off.p, (size_t)(nb + 1) * sizeof(int64_t), cudaMemcpyDeviceToHost,
+                            s.stream));
+    RH_CUDA(cudaMemcpyAsync(scores, s.scores.p, (size_t)nb * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    if (int rc = read_status(s)) return rc;
+    const int64_t n_tok = token_offsets[nb];
+    if (n_tok < 0 || n_tok > total) return fail(RH_ERR_CUDA, "CTC collapse produced an impossible token count");
+    if (n_tok > 0) {
+        RH_CUDA(cudaMemcpyAsync(tokens, s.tokens.p, (size_t)n_tok * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
+        RH_CUDA(cudaStreamSynchronize(s.stream));
+    }
+    return RH_OK;
+}
+
 // ------------------------------------------------------ recognition preprocessing
 // Target staged span when choosing a line's chunk (32 KB of shared memory per block); lines
 // that downscale so much that even one output column needs more than rh::kRecSpanMax input
@@ -972,23 +1095,14 @@ int rh_head_decode_kt(rh_ctx* ctx, const rh_weight* w, const float* x, int64_t b
     const int64_t rows = batch * t_len;
     if (rows == 0) return RH_OK;
     if (!x || !idx || !prob) return fail(RH_ERR_INVALID_ARG, "null input or output");
-    Slot& s = *ctx->slots[0];
-    std::lock_guard<std::mutex> lock(s.mu);
-    RH_CUDA(cudaSetDevice(s.device));
-    const rh_weight::Per* pw = weight_on(w, s.device);
-    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
-    const size_t x_bytes = (size_t)rows * (size_t)k * sizeof(float);
-    RH_CUDA(s.a.ensure(x_bytes));
-    RH_CUDA(s.idx.ensure((size_t)rows * sizeof(int32_t)));
-    RH_CUDA(s.prob.ensure((size_t)rows * sizeof(float)));
-    RH_CUDA(cudaMemcpyAsync(s.a.p, x, x_bytes, cudaMemcpyHostToDevice, s.stream));
-    if (int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, (int32_t*)s.idx.p, (float*)s.prob.p, nullptr,
-                              false, s.stream, t_len))
-        return rc;
-    RH_CUDA(cudaMemcpyAsync(idx, s.idx.p, (size_t)rows * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
-    RH_CUDA(cudaMemcpyAsync(prob, s.prob.p, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
-    RH_CUDA(cudaStreamSynchronize(s.stream));
-    return read_status(s);
+    // contiguous line shards of equal size (every line has t_len timesteps), one per device
+    const int nd = (int)ctx->slots.size();
+    return run_shards(nd, [&](int d, int slot) -> int {
+        const int64_t b0 = batch * d / nd, b1 = batch * (d + 1) / nd;
+        if (b1 <= b0) return RH_OK;
+        return kt_on_slot(ctx, w, slot, x + (size_t)b0 * (size_t)k * (size_t)t_len, b1 - b0, t_len,
+                          idx + b0 * t_len, prob + b0 * t_len);
+    });
 }
 
 int rh_head_decode_kt_ctc(rh_ctx* ctx, const rh_weight* w, const float* x, int64_t batch, int64_t k, int64_t t_len,
@@ -1003,60 +1117,36 @@ int rh_head_decode_kt_ctc(rh_ctx* ctx, const rh_weight* w, const float* x, int64
     token_offsets[0] = 0;
     if (batch == 0) return RH_OK;
     if (!valid_t || !scores) return fail(RH_ERR_INVALID_ARG, "null valid lengths or scores");
-    std::vector<int64_t> ranges(2 * (size_t)batch);  // line starts, then line ends (rows of the batch)
-    int64_t total = 0;
+    std::vector<int64_t> vstart((size_t)batch + 1, 0);  // valid rows before each line
     for (int64_t b = 0; b < batch; ++b) {
         if (valid_t[b] < 0 || valid_t[b] > t_len)
             return fail(RH_ERR_INVALID_ARG, "valid length " + std::to_string(valid_t[b]) + " of line " +
                                                 std::to_string(b) + " is outside [0, " + std::to_string(t_len) + "]");
-        ranges[b] = b * t_len;
-        ranges[batch + b] = b * t_len + valid_t[b];
-        total += valid_t[b];
+        vstart[b + 1] = vstart[b] + valid_t[b];
     }
-    if (total == 0) {  // every line empty: no tokens, score 0
-        for (int64_t b = 0; b < batch; ++b) {
-            token_offsets[b + 1] = 0;
-            scores[b] = 0.0f;
-        }
-        return RH_OK;
+    if (vstart[batch] > 0 && (!x || !tokens)) return fail(RH_ERR_INVALID_ARG, "null input or tokens");
+    // contiguous line shards of equal size, one per device; shard d writes its tokens from its
+    // first valid row's position and the shards are packed back to back at the end
+    const int nd = (int)ctx->slots.size();
+    std::vector<std::vector<int64_t>> local_off(nd);
+    int rc = run_shards(nd, [&](int d, int slot) -> int {
+        const int64_t b0 = batch * d / nd, b1 = batch * (d + 1) / nd;
+        local_off[d].assign((size_t)(b1 - b0) + 1, 0);
+        if (b1 <= b0) return RH_OK;
+        return kt_ctc_on_slot(ctx, w, slot, x + (size_t)b0 * (size_t)k * (size_t)t_len, b1 - b0, t_len, valid_t + b0,
+                              tokens + vstart[b0], local_off[d].data(), scores + b0);
+    });
+    if (rc) return rc;
+    int64_t wpos = 0;
+    for (int d = 0; d < nd; ++d) {
+        const int64_t b0 = batch * d / nd, b1 = batch * (d + 1) / nd;
+        if (b1 <= b0) continue;
+        const int64_t n_tok = local_off[d][b1 - b0];
+        if (n_tok > 0 && vstart[b0] != wpos) std::memmove(tokens + wpos, tokens + vstart[b0], (size_t)n_tok * sizeof(int32_t));
+        for (int64_t b = b0; b < b1; ++b) token_offsets[b] = wpos + local_off[d][b - b0];
+        wpos += n_tok;
     }
-    if (!x || !tokens) return fail(RH_ERR_INVALID_ARG, "null input or tokens");
-    const int64_t rows = batch * t_len;
-    Slot& s = *ctx->slots[0];
-    std::lock_guard<std::mutex> lock(s.mu);
-    RH_CUDA(cudaSetDevice(s.device));
-    const rh_weight::Per* pw = weight_on(w, s.device);
-    if (!pw) return fail(RH_ERR_INVALID_ARG, "weight was not packed for this context's devices");
-    const size_t x_bytes = (size_t)rows * (size_t)k * sizeof(float);
-    RH_CUDA(s.a.ensure(x_bytes));
-    RH_CUDA(s.idx.ensure((size_t)rows * sizeof(int32_t)));
-    RH_CUDA(s.prob.ensure((size_t)rows * sizeof(float)));
-    RH_CUDA(s.lines.ensure(ranges.size() * sizeof(int64_t)));
-    RH_CUDA(s.tok_off.ensure((size_t)(batch + 1) * sizeof(int64_t)));
-    RH_CUDA(s.tokens.ensure((size_t)total * sizeof(int32_t)));
-    RH_CUDA(s.scores.ensure((size_t)batch * sizeof(float)));
-    RH_CUDA(cudaMemcpyAsync(s.a.p, x, x_bytes, cudaMemcpyHostToDevice, s.stream));
-    if (int rc = enqueue_head(ctx, w, s, *pw, (const float*)s.a.p, rows, (int32_t*)s.idx.p, (float*)s.prob.p, nullptr,
-                              false, s.stream, t_len))
-        return rc;
-    RH_CUDA(cudaMemcpyAsync(s.lines.p, ranges.data(), ranges.size() * sizeof(int64_t), cudaMemcpyHostToDevice,
-                            s.stream));
-    const int64_t* d_begin = (const int64_t*)s.lines.p;
-    RH_CUDA(rh::launch_ctc_collapse((const int32_t*)s.idx.p, (const float*)s.prob.p, d_begin, batch,
-                                    (int32_t*)s.tokens.p, (int64_t*)s.tok_off.p, (float*)s.scores.p, s.stream,
-                                    d_begin + batch));
-    s.launches += 3;
-    RH_CUDA(cudaMemcpyAsync(token_offsets, s.tok_off.p, (size_t)(batch + 1) * sizeof(int64_t), cudaMemcpyDeviceToHost,
-                            s.stream));
-    RH_CUDA(cudaMemcpyAsync(scores, s.scores.p, (size_t)batch * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
-    RH_CUDA(cudaStreamSynchronize(s.stream));
-    if (int rc = read_status(s)) return rc;
-    const int64_t n_tok = token_offsets[batch];
-    if (n_tok < 0 || n_tok > total) return fail(RH_ERR_CUDA, "CTC collapse produced an impossible token count");
-    if (n_tok > 0) {
-        RH_CUDA(cudaMemcpyAsync(tokens, s.tokens.p, (size_t)n_tok * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
-        RH_CUDA(cudaStreamSynchronize(s.stream));
-    }
+    token_offsets[batch] = wpos;
     return RH_OK;
 }
 

@@ -886,3 +886,36 @@ def test_multi_device_shards_and_redispatch(rh, oracle, monkeypatch):
         # the failed shard is redone on device 0 with the same plan: identical results
         assert np.array_equal(idx2, idx) and np.array_equal(prob2, prob)
         qw.free()
+
+
+@pytest.mark.skipif("__import__('torch').cuda.device_count() < 2")
+def test_multi_device_svtr_layout_and_padded_batch(rh, monkeypatch):
+    """The [batch, K, T] entry points shard their lines over the context's devices: results
+    agree with one device (prob to the last bits of a different split plan), and a failed
+    shard is redone on a healthy device with identical results."""
+    from rust_ppocrv6_b200 import workloads
+
+    wl = workloads.make(0)
+    rng = np.random.default_rng(83)
+    B, T = 11, 57
+    x = rng.standard_normal((B, wl.w_t.shape[1], T), dtype=np.float32)
+    valid = rng.integers(0, T + 1, B).astype(np.int64)
+    with rh.Context(devices=[0]) as c1:
+        qw1 = rh.QuantizedWeight.from_f32_transposed(wl.w_t, ctx=c1, bias=wl.bias)
+        idx1, prob1 = rh.head_decode_kt(x, qw1)
+        tok1, off1, sc1 = rh.head_decode_kt_ctc(x, qw1, valid)
+        qw1.free()
+    with rh.Context(devices=[0, 1]) as c:
+        qw = rh.QuantizedWeight.from_f32_transposed(wl.w_t, ctx=c, bias=wl.bias)
+        idx, prob = rh.head_decode_kt(x, qw)
+        tok, off, sc = rh.head_decode_kt_ctc(x, qw, valid)
+        assert np.array_equal(idx, idx1)
+        np.testing.assert_allclose(prob, prob1, rtol=2e-6)
+        assert np.array_equal(tok, tok1) and np.array_equal(off, off1)
+        np.testing.assert_allclose(sc, sc1, rtol=2e-6)
+        monkeypatch.setenv("RH_FAULT_DEVICE", "1")
+        idx2, prob2 = rh.head_decode_kt(x, qw)
+        tok2, off2, sc2 = rh.head_decode_kt_ctc(x, qw, valid)
+        assert np.array_equal(idx2, idx) and np.array_equal(prob2, prob)
+        assert np.array_equal(tok2, tok) and np.array_equal(off2, off) and np.array_equal(sc2, sc)
+        qw.free()
