@@ -1028,43 +1028,12 @@ int rh_head_decode_lines(rh_ctx* ctx, const rh_weight* w, const float* a, const 
         while (l < n_lines && line_offsets[l] < target) ++l;
         cut[d] = std::max(cut[d - 1], std::min(line_offsets[l], r0 + total));
     }
-    const std::vector<int> faults = injected_fault_slots();
-    std::vector<int> rc(nd, RH_OK);
-    std::vector<std::string> msg(nd);
-    auto run = [&](int d, int on_slot) {
+    return run_shards(nd, [&](int d, int slot) -> int {
         const int64_t rows = cut[d + 1] - cut[d];
-        if (rows <= 0) return;
-        if (std::find(faults.begin(), faults.end(), on_slot) != faults.end()) {
-            rc[d] = RH_ERR_DEVICE_FAULT;
-            msg[d] = "injected failure on slot " + std::to_string(on_slot);
-            return;
-        }
-        rc[d] = run_host_on_slot(ctx, w, on_slot, a + (size_t)(cut[d] - r0) * (size_t)k, rows, idx + (cut[d] - r0),
-                                 prob + (cut[d] - r0), nullptr);
-        if (rc[d]) msg[d] = g_err;
-    };
-    if (nd == 1) {
-        run(0, 0);
-    } else {
-        std::vector<std::thread> th;
-        for (int d = 0; d < nd; ++d) th.emplace_back(run, d, d);
-        for (auto& t : th) t.join();
-    }
-    // Redo failed shards on a healthy device (results do not depend on the device).
-    int healthy = -1;
-    for (int d = 0; d < nd; ++d)
-        if (rc[d] == RH_OK && std::find(faults.begin(), faults.end(), d) == faults.end()) {
-            healthy = d;
-            break;
-        }
-    for (int d = 0; d < nd; ++d) {
-        if (rc[d] == RH_OK) continue;
-        if (rc[d] == RH_ERR_INVALID_ARG) return fail(rc[d], msg[d]);
-        if (healthy < 0) return fail(RH_ERR_DEVICE_FAULT, "every device shard failed; last: " + msg[d]);
-        run(d, healthy);
-        if (rc[d] != RH_OK) return fail(rc[d], msg[d]);
-    }
-    return RH_OK;
+        if (rows <= 0) return RH_OK;
+        return run_host_on_slot(ctx, w, slot, a + (size_t)(cut[d] - r0) * (size_t)k, rows, idx + (cut[d] - r0),
+                                prob + (cut[d] - r0), nullptr);
+    });
 }
 
 int rh_head_decode_kt_device(rh_ctx* ctx, const rh_weight* w, int slot, const float* d_x, int64_t batch,
@@ -1286,45 +1255,17 @@ int rh_head_decode_ctc(rh_ctx* ctx, const rh_weight* w, const float* a, const in
         while (l < n_lines && line_offsets[l] < target) ++l;
         lcut[d] = l;
     }
-    const std::vector<int> faults = injected_fault_slots();
-    std::vector<int> rc(nd, RH_OK);
-    std::vector<std::string> msg(nd);
     std::vector<std::vector<int64_t>> local_off(nd);
-    auto run = [&](int d, int on_slot) {
+    int rc = run_shards(nd, [&](int d, int slot) -> int {
         const int64_t l0 = lcut[d], l1 = lcut[d + 1];
-        if (l1 <= l0) return;
-        if (std::find(faults.begin(), faults.end(), on_slot) != faults.end()) {
-            rc[d] = RH_ERR_DEVICE_FAULT;
-            msg[d] = "injected failure on slot " + std::to_string(on_slot);
-            return;
-        }
+        local_off[d].assign((size_t)(l1 - l0) + 1, 0);
+        if (l1 <= l0) return RH_OK;
         std::vector<int64_t> lo(l1 - l0 + 1);
         for (int64_t l = l0; l <= l1; ++l) lo[l - l0] = line_offsets[l] - line_offsets[l0];
-        local_off[d].assign(l1 - l0 + 1, 0);
-        rc[d] = run_ctc_on_slot(ctx, w, on_slot, a + (size_t)(line_offsets[l0] - r0) * (size_t)k, lo.data(), l1 - l0,
-                                tokens + (line_offsets[l0] - r0), local_off[d].data(), scores + l0);
-        if (rc[d]) msg[d] = g_err;
-    };
-    if (nd == 1) {
-        run(0, 0);
-    } else {
-        std::vector<std::thread> th;
-        for (int d = 0; d < nd; ++d) th.emplace_back(run, d, d);
-        for (auto& t : th) t.join();
-    }
-    int healthy = -1;
-    for (int d = 0; d < nd; ++d)
-        if (rc[d] == RH_OK && std::find(faults.begin(), faults.end(), d) == faults.end()) {
-            healthy = d;
-            break;
-        }
-    for (int d = 0; d < nd; ++d) {
-        if (rc[d] == RH_OK) continue;
-        if (rc[d] == RH_ERR_INVALID_ARG) return fail(rc[d], msg[d]);
-        if (healthy < 0) return fail(RH_ERR_DEVICE_FAULT, "every device shard failed; last: " + msg[d]);
-        run(d, healthy);
-        if (rc[d] != RH_OK) return fail(rc[d], msg[d]);
-    }
+        return run_ctc_on_slot(ctx, w, slot, a + (size_t)(line_offsets[l0] - r0) * (size_t)k, lo.data(), l1 - l0,
+                               tokens + (line_offsets[l0] - r0), local_off[d].data(), scores + l0);
+    });
+    if (rc) return rc;
     // pack the shards' tokens back to back (each shard's tokens sit at the start of its rows)
     int64_t wpos = 0;
     for (int d = 0; d < nd; ++d) {
