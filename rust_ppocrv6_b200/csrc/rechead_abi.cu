@@ -1375,24 +1375,10 @@ int rh_rec_preprocess(rh_ctx* ctx, const uint8_t* rgb, int64_t rgb_len, const in
     if (rgb_len > 0 && !rgb) return fail(RH_ERR_INVALID_ARG, "null pixel buffer");
     // contiguous line shards of equal size (every line has the same output size), one per device
     const int nd = (int)ctx->slots.size();
-    std::vector<int64_t> cut(nd + 1);
-    for (int d = 0; d <= nd; ++d) cut[d] = n_lines * d / nd;
-    std::vector<int> rc(nd, RH_OK);
-    std::vector<std::string> msg(nd);
-    auto run = [&](int d) {
-        rc[d] = rec_host_on_slot(ctx, d, rgb, rgb_offsets, widths, heights, cut[d], cut[d + 1], b, out);
-        if (rc[d]) msg[d] = g_err;
-    };
-    if (nd == 1) {
-        run(0);
-    } else {
-        std::vector<std::thread> th;
-        for (int d = 0; d < nd; ++d) th.emplace_back(run, d);
-        for (auto& t : th) t.join();
-    }
-    for (int d = 0; d < nd; ++d)
-        if (rc[d]) return fail(rc[d], msg[d]);
-    return RH_OK;
+    return run_shards(nd, [&](int d, int slot) -> int {
+        return rec_host_on_slot(ctx, slot, rgb, rgb_offsets, widths, heights, n_lines * d / nd, n_lines * (d + 1) / nd,
+                                b, out);
+    });
 }
 
 int rh_rec_preprocess_device(rh_ctx* ctx, int slot, const uint8_t* d_rgb, int64_t rgb_len, const int64_t* rgb_offsets,

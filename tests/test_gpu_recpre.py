@@ -140,17 +140,21 @@ def test_argument_errors_are_reported_before_any_launch(rh, ctx):
     assert ctx.launch_count() == before
 
 
-def test_sharded_over_every_device(rh, oracle):
+def test_sharded_over_every_device(rh, oracle, monkeypatch):
     import torch
 
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("one device")
     crops = crops_of(MIXED * 3, 16)
+    ref, _ = oracle.rec_preprocess_batch(crops, threads=8)
     with rh.Context(list(range(n))) as c:
         got, _ = rh.RecPreprocess(ctx=c).process_batch(crops)
-    ref, _ = oracle.rec_preprocess_batch(crops, threads=8)
-    assert_same(got, ref, f"{n} devices")
+        assert_same(got, ref, f"{n} devices")
+        # a shard whose device fails (injected on the host) is redone on a healthy device
+        monkeypatch.setenv("RH_FAULT_DEVICE", "1")
+        got2, _ = rh.RecPreprocess(ctx=c).process_batch(crops)
+        assert_same(got2, ref, f"{n} devices, slot 1 failed")
 
 
 def test_crops_out_of_order_shared_and_in_a_larger_buffer(rh, ctx, oracle):
