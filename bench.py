@@ -65,6 +65,7 @@ def parse():
                     help="int8: the quantised head (the metric's path); f32: the engine's default FP32 head")
     ap.add_argument("--cpu-sample-lines", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-strong", action="store_true", help="skip the cfg3 strong-scaling sub-record")
     return ap.parse_args()
 
 
@@ -199,16 +200,40 @@ def measured_hbm_gbs():
         return 6650.0, "fallback 6.65 TB/s"
 
 
-def profiled_traffic():
-    """DRAM bytes (read + write) of one cfg2 head-kernel launch, from the committed ncu summary."""
-    import re
+KERNEL_SOURCES = ("rust_ppocrv6_b200/csrc/rechead_kernels.cu", "rust_ppocrv6_b200/csrc/sm100_ptx.cuh",
+                  "rust_ppocrv6_b200/csrc/head_params.h")
+TRAFFIC_RECORD = os.path.join(ROOT, "profiles", "head_kernel_traffic.json")
 
+
+def kernel_source_sha16() -> str:
+    """First 16 hex digits of the SHA-256 over the head kernel's source files: a DRAM-traffic
+    figure captured by ncu applies only to the kernel built from the same sources."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for rel in KERNEL_SOURCES:
+        with open(os.path.join(ROOT, rel), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
+
+
+def profiled_traffic(workload: str = "cfg2", weights: str = "int8"):
+    """(DRAM bytes read + written per head-kernel launch, description) from the ncu capture
+    recorded for this workload and these kernel sources, or (None, reason) when the kernel
+    changed since the capture or none was recorded."""
     try:
-        with open(os.path.join(ROOT, "profiles", "head_kernel_cfg2_ncu_full.md")) as f:
-            m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", f.read(), re.M)
-        return int(m.group(1)) if m else None
-    except OSError:
-        return None
+        with open(TRAFFIC_RECORD) as f:
+            records = json.load(f)["records"]
+    except (OSError, ValueError, KeyError):
+        return None, "no ncu capture recorded"
+    sha = kernel_source_sha16()
+    for r in records:
+        if r.get("workload") == workload and r.get("weights") == weights:
+            if r.get("kernel_source_sha16") != sha:
+                return None, f"the ncu capture is of kernel sources {r.get('kernel_source_sha16')}, not {sha}"
+            return int(r["dram_bytes_per_launch"]), (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                                     f"{r.get('kernel', 'head_kernel')} launch on {workload}")
+    return None, f"no ncu capture recorded for {workload}/{weights}"
 
 
 def cpu_reference(lines_off: np.ndarray, x: np.ndarray, w_t, bias, sample_lines: int, target_s: float = 10.0):
@@ -292,30 +317,34 @@ def run_reference_arm(args, world, rank):
             "e2e": {"value": v, "unit": RECPRE_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }), flush=True)
         return
-    if args.weights == "f32":
-        print(json.dumps({"impl": "reference", "unavailable": "the CPU arm times the quantised (int8) head of the "
-                          "metric; the FP32 head has no CPU port here"}), flush=True)
-        return
     off, rows, _, desc, _ = workload_for(args.workload, 1, 0)
     w_t, bias = head_weights(args.workload)
     x = synth(min(rows, int(off[min(args.cpu_sample_lines, off.size - 1)])), 1234, w_t.shape[1])
     from oracle import oracle
 
-    q, s = oracle.pack(w_t)
     nl = min(args.cpu_sample_lines, off.size - 1)
     soff = off[:nl + 1]
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    if args.weights == "f32":  # matmul_transposed_b's register-blocked AVX2 kernel restated
+        def one():
+            oracle.head_decode_f32(x, soff, w_t, bias, threads=threads)
+    else:
+        q, s = oracle.pack(w_t)
+
+        def one():
+            oracle.head_decode(x, soff, q, s, bias, threads=threads)
     for _ in range(max(args.warmup, 0)):
-        oracle.head_decode(x, soff, q, s, bias, threads=threads)
+        one()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.head_decode(x, soff, q, s, bias, threads=threads)
+        one()
     dt = time.perf_counter() - t0
     srows = int(soff[-1])
     value = srows * args.steps / dt
     sample = f"{nl} lines x T=120 ({srows} timesteps) of {desc.split(';')[0]} per step"
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC if args.weights == "int8" else METRIC_F32, "value": value,
+        "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
         "higher_is_better": True, "scaling": "none (host CPU)", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) features, N(0,0.05^2) weights, N(0,0.01^2) bias)",
@@ -445,6 +474,9 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        # the host-side gather of the strong-scaling record's idx/prob (host arrays, as the
+        # reference's per-line fan-out returns them)
+        host_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
 
     def barrier():
         if dist is not None:
@@ -457,6 +489,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if world == 1:
+        host_group = None
     if args.workload == "recpre":
         run_recpre(args, world, rank, local, torch, rh, barrier, max_over_ranks)
         if dist is not None:
@@ -534,18 +568,22 @@ def main():
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
     e2e_value = global_rows * args.steps / e2e_s
+    # the link the e2e leg crosses: a bare pinned H2D copy of one step's features
+    h2d_gbs = h2d_bandwidth(torch, x_pin, xs[0], stream)
 
     # roofline of the dominant kernel (the fused head; the split merge is <1 % of a step)
     peak, peak_src = measured_peak_tflops()
     achieved = 2 * k_dim * n_classes * rows / (dev_ms / args.steps / 1e3) / 1e12  # 2*K*N per timestep
-    traffic = profiled_traffic()
+    traffic, traffic_src = profiled_traffic(args.workload, args.weights)
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "peak_source": peak_src,
-                "traffic": traffic if args.workload == "cfg2" and args.weights == "int8" else None,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one cfg2 launch "
-                                  "(profiles/head_kernel_cfg2_ncu_full.md)",
+                "traffic": traffic, "traffic_source": traffic_src,
                 "tf32_equiv_frac": achieved / (peak / 2),
                 "note": "achieved = 2*K*N*rows per step / device time per step (head + merge kernels)"}
+
+    strong = None
+    if args.workload == "cfg2" and not args.no_strong:
+        strong = strong_record(args, world, rank, local, torch, rh, ctx, qw, barrier, max_over_ranks, host_group)
 
     out = {
         "metric": METRIC if args.weights == "int8" else METRIC_F32, "value": value, "unit": UNIT, "n_gpus": world,
@@ -556,12 +594,18 @@ def main():
         "config": {"workload": desc, "timesteps_per_step": global_rows, "parallelism": f"lines sharded x{world}",
                    "l2": f"inputs rotate over {n_copies} device copies ({n_copies * x_bytes / 2**20:.0f} MiB > 2x L2)"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x_bytes),
-                "d2h_bytes_per_step": int(rows * 8), "ms_per_step": e2e_s * 1e3 / args.steps},
+                "d2h_bytes_per_step": int(rows * 8), "ms_per_step": e2e_s * 1e3 / args.steps,
+                "h2d_gbs_measured": h2d_gbs,
+                "link_bound_value": global_rows / (x_bytes / (h2d_gbs * 1e9)) if h2d_gbs else None,
+                "note": "rh_head_decode from pinned host memory; link_bound_value = the rate if every step took "
+                        "only its features' H2D at the measured bare-copy bandwidth"},
         "gpu_launches": int(launches),
         "roofline": roofline,
         "clocks": clocks.summary(),
         "checksum": output_checksum(idx, prob),
     }
+    if strong is not None:
+        out["strong"] = strong
     if args.weights == "f32":
         out["config"]["weights"] = "f32 (hi/lo fp16 images, 23 MMA K-steps per tile)"
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.weights == "int8":
@@ -575,6 +619,124 @@ def main():
         print(json.dumps(out), flush=True)
     if dist is not None:
         dist.destroy_process_group()
+
+
+def h2d_bandwidth(torch, src_pinned, dst, stream, reps: int = 5):
+    """GB/s of a bare pinned host -> device copy of `src_pinned` (best of `reps`, CUDA events)."""
+    best = None
+    for _ in range(reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dst.copy_(src_pinned, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    return src_pinned.numel() * src_pinned.element_size() / (best / 1e3) / 1e9 if best else None
+
+
+def strong_record(args, world, rank, local, torch, rh, ctx, qw, barrier, max_over_ranks, host_group):
+    """cfg3 (one 8192-line ragged batch, ~528k timesteps) sharded over the N ranks by balanced
+    timestep counts: device-resident time (max over ranks) and end to end through
+    rh_head_decode_lines from pinned host memory with every rank's idx/prob gathered to rank 0's
+    host memory (gloo) inside the timed region."""
+    import ctypes
+
+    from rust_ppocrv6_b200 import workloads
+
+    off_all = workloads.ragged_offsets(np.random.default_rng(workloads.SEED + 3), 8192)
+    total = int(off_all[-1])
+    cuts = [workloads.shard_lines(off_all, world, r) for r in range(world)]
+    shard_rows = [int(off_all[l1] - off_all[l0]) for l0, l1 in cuts]
+    l0, l1 = cuts[rank]
+    r0, rows = int(off_all[l0]), shard_rows[rank]
+    off = np.ascontiguousarray(off_all[l0:l1 + 1] - off_all[l0])
+    x_all = synth(total, 3000, K_DIM)  # the same global batch on every rank
+    x = np.ascontiguousarray(x_all[r0:r0 + rows])
+    k_dim = x.shape[1]
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    n_copies = max(2, int(np.ceil(2 * L2_BYTES / max(x.nbytes, 1))) + 1) if rows else 1
+    xs = [torch.from_numpy(x).cuda()]
+    for i in range(1, min(n_copies, 64)):
+        xs.append(xs[0].roll(i, dims=0).contiguous())
+    n_copies = len(xs)
+    d_idx = torch.empty(max(rows, 1), dtype=torch.int32, device="cuda")
+    d_prob = torch.empty(max(rows, 1), dtype=torch.float32, device="cuda")
+
+    def dev_step(i):
+        if rows:
+            rh.head_decode_device(qw, xs[i % n_copies].data_ptr(), rows, d_idx.data_ptr(), d_prob.data_ptr(), sptr)
+
+    for i in range(max(3, args.warmup)):
+        dev_step(i)
+    torch.cuda.synchronize()
+    ctx.sync()
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        dev_step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ctx.sync()
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    barrier()
+
+    # end to end: host features in, every rank's results in rank 0's host arrays out
+    lib = rh.load()
+    vp = ctypes.c_void_p
+    x_pin = torch.from_numpy(x).pin_memory()
+    max_rows = max(shard_rows)
+    pack = torch.zeros(2 * max_rows, dtype=torch.int32).pin_memory()  # idx then prob bits
+    gathered = [torch.empty(2 * max_rows, dtype=torch.int32) for _ in range(world)] if rank == 0 else None
+    idx_all = np.empty(total, np.int32)
+    prob_all = np.empty(total, np.float32)
+
+    def e2e_step():
+        if rows:
+            rh._lib.check(lib.rh_head_decode_lines(ctx.handle, qw.handle, vp(x_pin.data_ptr()),
+                                                   off.ctypes.data_as(vp), off.size - 1, k_dim,
+                                                   vp(pack.data_ptr()), vp(pack.data_ptr() + 4 * max_rows)))
+        if host_group is None:
+            idx_all[:] = pack[:rows].numpy()
+            prob_all[:] = pack[max_rows:max_rows + rows].numpy().view(np.float32)
+            return
+        import torch.distributed as dist
+
+        dist.gather(pack, gathered, dst=0, group=host_group)
+        if rank == 0:
+            for r, (a, b) in enumerate(cuts):
+                g0, n = int(off_all[a]), shard_rows[r]
+                idx_all[g0:g0 + n] = gathered[r][:n].numpy()
+                prob_all[g0:g0 + n] = gathered[r][max_rows:max_rows + n].numpy().view(np.float32)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    import zlib
+
+    return {
+        "workload": f"cfg3: 8192 ragged lines T~U{{10..120}} (M={total}), K=120, N=18710, sharded by balanced "
+                    f"timestep counts over {world} GPU(s)",
+        "scaling": "strong", "timesteps_per_step": total, "rows_per_rank": shard_rows,
+        "value": total * args.steps / (dev_ms / 1e3), "unit": UNIT, "ms_per_step": dev_ms / args.steps,
+        "l2": f"inputs rotate over {n_copies} device copies per rank",
+        "e2e": {"value": total * args.steps / e2e_s, "unit": UNIT, "ms_per_step": e2e_s * 1e3 / args.steps,
+                "h2d_bytes_per_step": int(total * k_dim * 4), "d2h_bytes_per_step": int(total * 8),
+                "gather": "each rank: rh_head_decode_lines on its shard (pinned host memory); then idx/prob "
+                          "of every rank gathered into rank 0's host arrays (gloo)" if world > 1 else
+                          "rh_head_decode_lines on the whole batch (pinned host memory)"},
+        "idx_crc32": f"{zlib.crc32(idx_all.tobytes()):08x}" if rank == 0 else None,
+    }
 
 
 if __name__ == "__main__":

@@ -58,6 +58,9 @@ def lib() -> ctypes.CDLL:
     L.oracle_head_decode_one_line.argtypes = [_f32p, _i64, _i64, _i8p, _f32p, _i64, _vp, _i32p, _f32p, _f32p,
                                               _int, _int]
     L.oracle_matmul_f32_transposed_b.argtypes = [_f32p, _i64, _i64, _f32p, _i64, _vp, _f32p]
+    L.oracle_matmul_transposed_b.argtypes = [_f32p, _i64, _i64, _f32p, _i64, _vp, _f32p, _int]
+    L.oracle_head_decode_f32.argtypes = [_f32p, _i64p, _i64, _i64, _f32p, _i64, _vp, _i32p, _f32p, _vp, _vp, _int,
+                                         _int]
     L.oracle_exp_poly.argtypes = [ctypes.c_float]
     L.oracle_exp_poly.restype = ctypes.c_float
     _u32 = ctypes.c_uint32
@@ -225,6 +228,49 @@ def matmul_f32_transposed_b(a, b_t, bias=None):
     out = np.empty(a.shape[:-1] + (n,), np.float32)
     b = None if bias is None else _c(bias, np.float32)
     lib().oracle_matmul_f32_transposed_b(a.reshape(rows, k), rows, k, b_t, n, _ptr(b), out.reshape(rows, n))
+    return out
+
+
+def matmul_transposed_b(a, b_t, bias=None, use_avx2: bool = True):
+    """matmul_transposed_b (src/ops/matmul.rs:514-897) as a recognition worker runs it
+    (ScopedDisableParallel: register-blocked tiles of 3 rows x 4 columns, the n % 4 tail
+    columns through avx2_dot_product). a [..., k] -> [..., n]; raises ValueError where the
+    reference returns OperatorError (inner dimension :531-536, bias length :585-593)."""
+    a = _c(a, np.float32)
+    b_t = _c(b_t, np.float32)
+    n, k = b_t.shape
+    if a.shape[-1] != k:
+        raise ValueError(f"MatMulTransposedB: Inner dimensions must match: {a.shape[-1]} != {k}")
+    b = None if bias is None else _c(bias, np.float32).reshape(-1)
+    if b is not None and b.size != n:
+        raise ValueError(f"MatMulTransposedB: bias has {b.size} elements but n is {n}")
+    rows = int(np.prod(a.shape[:-1])) if a.ndim > 1 else 1
+    out = np.empty(a.shape[:-1] + (n,), np.float32)
+    lib().oracle_matmul_transposed_b(a.reshape(rows, k), rows, k, b_t, n, _ptr(b), out.reshape(rows, n),
+                                     int(use_avx2))
+    return out
+
+
+def head_decode_f32(a, line_offsets, w_t, bias, threads=1, use_avx2=True, want_logits=False, want_gap=False):
+    """The FP32 head per timestep row: MatMul.12 through matmul_transposed_b (+ folded bias)
+    -> Softmax.2 -> argmax; the same dict as head_decode."""
+    a = _c(a, np.float32)
+    off = _c(line_offsets, np.int64)
+    w_t = _c(w_t, np.float32)
+    n, k = w_t.shape
+    m = a.shape[0]
+    idx = np.empty(m, np.int32)
+    prob = np.empty(m, np.float32)
+    logits = np.empty((m, n), np.float32) if want_logits else None
+    gap = np.empty(m, np.float32) if want_gap else None
+    b = None if bias is None else _c(bias, np.float32)
+    lib().oracle_head_decode_f32(a, off, off.size - 1, k, w_t, n, _ptr(b), idx, prob, _ptr(logits), _ptr(gap),
+                                 int(threads), int(use_avx2))
+    out = {"idx": idx, "prob": prob}
+    if want_logits:
+        out["logits"] = logits
+    if want_gap:
+        out["gap"] = gap
     return out
 
 

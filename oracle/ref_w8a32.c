@@ -671,3 +671,235 @@ void oracle_matmul_f32_transposed_b(const float *a, int64_t rows, int64_t k, con
             out[r * n + j] = (float)acc + (bias ? bias[j] : 0.0f);
         }
 }
+
+/* ------------------------------------------------------- FP32 head (matmul_transposed_b) */
+
+/*
+ * The engine's default head (OcrEngineConfig.quantize_rec_head = false, src/pipeline.rs:59):
+ * MatMul.12 runs matmul_transposed_b (src/ops/matmul.rs:514-897) on the FP32 [n][k] weight.
+ * A recognition line runs inside a rec worker with ScopedDisableParallel
+ * (src/pipeline.rs:417-427), so neither parallel branch is taken: with AVX2 and k % 8 == 0
+ * the rows go through run_block (:648-742) in groups of TILE_ROWS = 3 (:1094), columns
+ * 0..n - n%4 through transposed_b_tile_fma (:1025-1087) and the last n % 4 columns through
+ * compute_transposed_b_cols_avx2 (:913-1000), which for fewer than 4 columns is
+ * avx2_dot_product (:1120-1160); otherwise each row goes through
+ * compute_transposed_b_cols_avx2 (AVX2) or compute_transposed_b_cols_scalar (:1097-1116).
+ */
+
+/* avx2_dot_product: src/ops/matmul.rs:1120-1160. */
+__attribute__((target("avx2,fma"))) static float f32_dot_avx2(const float *a, const float *b, int64_t n) {
+    int64_t i = 0;
+    __m256 v0 = _mm256_setzero_ps(), v1 = _mm256_setzero_ps(), v2 = _mm256_setzero_ps(), v3 = _mm256_setzero_ps();
+    while (i + 32 <= n) {
+        v0 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i), v0);
+        v1 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 8), _mm256_loadu_ps(b + i + 8), v1);
+        v2 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 16), _mm256_loadu_ps(b + i + 16), v2);
+        v3 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 24), _mm256_loadu_ps(b + i + 24), v3);
+        i += 32;
+    }
+    v0 = _mm256_add_ps(_mm256_add_ps(v0, v1), _mm256_add_ps(v2, v3));
+    while (i + 8 <= n) {
+        v0 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i), v0);
+        i += 8;
+    }
+    float sum = hsum256(v0);
+    while (i < n) {
+        sum += a[i] * b[i];
+        i++;
+    }
+    return sum;
+}
+
+/* compute_transposed_b_cols_avx2: src/ops/matmul.rs:913-1000 (columns col_start .. +count). */
+__attribute__((target("avx2,fma"))) static void f32_cols_avx2(const float *a_row, const float *b_t, const float *bias,
+                                                             float *out, int64_t col_start, int64_t col_count,
+                                                             int64_t k) {
+    int64_t c = 0;
+    while (c + 4 <= col_count) {
+        const int64_t j0 = col_start + c;
+        const float *b0 = b_t + j0 * k, *b1 = b0 + k, *b2 = b1 + k, *b3 = b2 + k;
+        __m256 acc0 = _mm256_setzero_ps(), acc1 = _mm256_setzero_ps(), acc2 = _mm256_setzero_ps(),
+               acc3 = _mm256_setzero_ps();
+        int64_t i = 0;
+        while (i + 8 <= k) {
+            __m256 va = _mm256_loadu_ps(a_row + i);
+            acc0 = _mm256_fmadd_ps(va, _mm256_loadu_ps(b0 + i), acc0);
+            acc1 = _mm256_fmadd_ps(va, _mm256_loadu_ps(b1 + i), acc1);
+            acc2 = _mm256_fmadd_ps(va, _mm256_loadu_ps(b2 + i), acc2);
+            acc3 = _mm256_fmadd_ps(va, _mm256_loadu_ps(b3 + i), acc3);
+            i += 8;
+        }
+        float s0 = hsum256(acc0), s1 = hsum256(acc1), s2 = hsum256(acc2), s3 = hsum256(acc3);
+        while (i < k) {
+            const float av = a_row[i];
+            s0 += av * b0[i];
+            s1 += av * b1[i];
+            s2 += av * b2[i];
+            s3 += av * b3[i];
+            i++;
+        }
+        if (bias) {
+            out[c] = s0 + bias[j0];
+            out[c + 1] = s1 + bias[j0 + 1];
+            out[c + 2] = s2 + bias[j0 + 2];
+            out[c + 3] = s3 + bias[j0 + 3];
+        } else {
+            out[c] = s0;
+            out[c + 1] = s1;
+            out[c + 2] = s2;
+            out[c + 3] = s3;
+        }
+        c += 4;
+    }
+    while (c < col_count) {
+        const int64_t j = col_start + c;
+        const float dot = f32_dot_avx2(a_row, b_t + j * k, k);
+        out[c] = bias ? dot + bias[j] : dot;
+        c++;
+    }
+}
+
+/* compute_transposed_b_cols_scalar: src/ops/matmul.rs:1097-1116 (Rust's f32 Sum folds from -0.0). */
+static void f32_cols_scalar(const float *a_row, const float *b_t, const float *bias, float *out, int64_t col_start,
+                            int64_t col_count, int64_t k) {
+    for (int64_t c = 0; c < col_count; c++) {
+        const int64_t j = col_start + c;
+        const float *b = b_t + j * k;
+        float dot = -0.0f;
+        for (int64_t i = 0; i < k; i++) dot += a_row[i] * b[i];
+        out[c] = bias ? dot + bias[j] : dot;
+    }
+}
+
+/* transposed_b_tile_fma<MR>: src/ops/matmul.rs:1025-1087; MR rows x 4 columns from column c. */
+__attribute__((target("avx2,fma"))) static void f32_tile(const float *a, const float *b, float *out, int64_t ldo,
+                                                        int64_t c, const float *bias, int64_t k, int mr) {
+    const float *b0 = b, *b1 = b + k, *b2 = b + 2 * k, *b3 = b + 3 * k;
+    __m256 acc[12];
+    for (int i = 0; i < 12; i++) acc[i] = _mm256_setzero_ps();
+    for (int64_t i = 0; i < k; i += 8) {
+        const __m256 bv0 = _mm256_loadu_ps(b0 + i), bv1 = _mm256_loadu_ps(b1 + i), bv2 = _mm256_loadu_ps(b2 + i),
+                     bv3 = _mm256_loadu_ps(b3 + i);
+        for (int r = 0; r < mr; r++) {
+            const __m256 av = _mm256_loadu_ps(a + r * k + i);
+            acc[r * 4] = _mm256_fmadd_ps(av, bv0, acc[r * 4]);
+            acc[r * 4 + 1] = _mm256_fmadd_ps(av, bv1, acc[r * 4 + 1]);
+            acc[r * 4 + 2] = _mm256_fmadd_ps(av, bv2, acc[r * 4 + 2]);
+            acc[r * 4 + 3] = _mm256_fmadd_ps(av, bv3, acc[r * 4 + 3]);
+        }
+    }
+    const __m128 bv = bias ? _mm_loadu_ps(bias + c) : _mm_setzero_ps();
+    for (int r = 0; r < mr; r++) {
+        const __m256 h01 = _mm256_hadd_ps(acc[r * 4], acc[r * 4 + 1]);
+        const __m256 h23 = _mm256_hadd_ps(acc[r * 4 + 2], acc[r * 4 + 3]);
+        const __m256 h0123 = _mm256_hadd_ps(h01, h23);
+        __m128 sums = _mm_add_ps(_mm256_castps256_ps128(h0123), _mm256_extractf128_ps(h0123, 1));
+        if (bias) sums = _mm_add_ps(sums, bv);
+        _mm_storeu_ps(out + r * ldo, sums);
+    }
+}
+
+/*
+ * Rows [0, rows) of one line (rows <= 3 when blocked; any count otherwise) into out [rows][n]:
+ * one run_block chunk (src/ops/matmul.rs:648-742) or run_row per row (:607-620).
+ */
+static void f32_line_rows(const float *a, int64_t rows, int64_t k, const float *b_t, int64_t n, const float *bias,
+                          float *out, int use_avx2) {
+    if (use_avx2 && k % 8 == 0) {
+        const int64_t cols_full = n - n % 4;
+        for (int64_t c = 0; c < cols_full; c += 4) f32_tile(a, b_t + c * k, out + c, n, c, bias, k, (int)rows);
+        if (cols_full < n)
+            for (int64_t r = 0; r < rows; r++)
+                f32_cols_avx2(a + r * k, b_t, bias, out + r * n + cols_full, cols_full, n - cols_full, k);
+        return;
+    }
+    for (int64_t r = 0; r < rows; r++) {
+        if (use_avx2)
+            f32_cols_avx2(a + r * k, b_t, bias, out + r * n, 0, n, k);
+        else
+            f32_cols_scalar(a + r * k, b_t, bias, out + r * n, 0, n, k);
+    }
+}
+
+/* matmul_transposed_b over the rows of one line (the engine's per-line call). */
+void oracle_matmul_transposed_b(const float *a, int64_t rows, int64_t k, const float *b_t, int64_t n,
+                                const float *bias, float *out, int use_avx2) {
+    const int64_t step = (use_avx2 && k % 8 == 0) ? 3 : (rows > 0 ? rows : 1);
+    for (int64_t r0 = 0; r0 < rows; r0 += step) {
+        const int64_t nr = rows - r0 < step ? rows - r0 : step;
+        f32_line_rows(a + r0 * k, nr, k, b_t, n, bias, out + r0 * n, use_avx2);
+    }
+}
+
+typedef struct {
+    const float *a; int64_t k, n; const float *b_t; const float *bias;
+    const int64_t *offsets; int64_t n_lines;
+    int32_t *idx; float *prob; float *logits_out; float *gap; int use_avx2;
+    atomic_long next;
+} f32_job;
+
+static void *f32_worker(void *p) {
+    f32_job *j = (f32_job *)p;
+    float *buf = (float *)malloc(sizeof(float) * (size_t)(3 * (j->n > 0 ? j->n : 1)));
+    float *prow = (float *)malloc(sizeof(float) * (size_t)(j->n > 0 ? j->n : 1));
+    for (;;) {
+        const int64_t l = atomic_fetch_add(&j->next, 1);
+        if (l >= j->n_lines) break;
+        const int64_t r_begin = j->offsets[l], r_end = j->offsets[l + 1];
+        const int64_t step = (j->use_avx2 && j->k % 8 == 0) ? 3 : 1;
+        for (int64_t r0 = r_begin; r0 < r_end; r0 += step) {
+            const int64_t nr = r_end - r0 < step ? r_end - r0 : step;
+            float *lg = j->logits_out ? j->logits_out + r0 * j->n : buf;
+            f32_line_rows(j->a + r0 * j->k, nr, j->k, j->b_t, j->n, j->bias, lg, j->use_avx2);
+            for (int64_t rr = 0; rr < nr; rr++) {
+                const int64_t r = r0 + rr;
+                const float *row = lg + rr * j->n;
+                if (j->gap) {
+                    float m1 = -INFINITY, m2 = -INFINITY;
+                    for (int64_t c = 0; c < j->n; c++) {
+                        const float v = row[c];
+                        if (v > m1) {
+                            m2 = m1;
+                            m1 = v;
+                        } else if (v > m2) {
+                            m2 = v;
+                        }
+                    }
+                    j->gap[r] = m1 - m2;
+                }
+                if (j->use_avx2)
+                    oracle_softmax_row_avx2(row, prow, j->n);
+                else
+                    oracle_softmax_row_scalar(row, prow, j->n);
+                int64_t mi;
+                float mv;
+                oracle_find_argmax(prow, j->n, j->use_avx2, &mi, &mv);
+                j->idx[r] = (int32_t)mi;
+                j->prob[r] = mv;
+            }
+        }
+    }
+    free(prow);
+    free(buf);
+    return NULL;
+}
+
+/*
+ * The FP32 head per timestep (matmul_transposed_b with the folded bias -> softmax ->
+ * find_argmax), lines handed to `threads` workers. Results do not depend on `threads`.
+ */
+int oracle_head_decode_f32(const float *a, const int64_t *line_offsets, int64_t n_lines, int64_t k, const float *b_t,
+                           int64_t n, const float *bias, int32_t *idx, float *prob, float *logits_out, float *gap,
+                           int threads, int use_avx2) {
+    if (n_lines <= 0) return OR_OK;
+    if (threads < 1) threads = 1;
+    f32_job j = {a, k, n, b_t, bias, line_offsets, n_lines, idx, prob, logits_out, gap, use_avx2, 0};
+    atomic_init(&j.next, 0);
+    int nt = threads > 256 ? 256 : threads;
+    if (nt > n_lines) nt = (int)n_lines;
+    pthread_t th[256];
+    for (int t = 1; t < nt; t++) pthread_create(&th[t], NULL, f32_worker, &j);
+    f32_worker(&j);
+    for (int t = 1; t < nt; t++) pthread_join(th[t], NULL);
+    return OR_OK;
+}

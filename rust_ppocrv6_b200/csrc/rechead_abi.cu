@@ -188,12 +188,12 @@ int check_ctx(rh_ctx* ctx) {
     return RH_OK;
 }
 
-// Enqueues the head (and the split merge) for rows [0, rows) of d_a on `stream`.
-int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per& pw, const float* d_a, int64_t rows,
-                 int32_t* d_idx, float* d_prob, float* d_logits, bool emit_logits, cudaStream_t stream,
-                 int64_t a_t = 0) {
-    if (rows <= 0) return RH_OK;
-    int n_mblocks, n_splits, cps, grid;
+// Launch parameters of the head over rows [0, rows) of d_a (a_t > 0: the [batch][k][a_t]
+// layout) with the planner's class-range split; `partial` is left for the caller to point at
+// its split scratch. Every head launch path builds its parameters here.
+rh::HeadParams head_params(rh_ctx* ctx, const rh_weight* w, const Slot& s, const rh_weight::Per& pw, const float* d_a,
+                           int64_t rows, int64_t a_t, int32_t* d_idx, float* d_prob, float* d_logits, int& grid) {
+    int n_mblocks, n_splits, cps;
     plan(rows, w->g.n_chunks, s.sms, n_mblocks, n_splits, cps, grid);
     rh::HeadParams p{};
     p.a = d_a;
@@ -216,28 +216,47 @@ int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per&
     p.idx = d_idx;
     p.prob = d_prob;
     p.logits = d_logits;
+    p.partial = nullptr;
     p.status = s.d_status;
     p.timeout_ns = ctx->timeout_ns;
     p.debug_flags = 0;
     if (const char* dbg = std::getenv("RH_DEBUG_FLAGS")) p.debug_flags = std::atoi(dbg);
-    if (!emit_logits && n_splits > 1) {
+    return p;
+}
+
+// Launches the head, then (fused, class range split) the merge of the per-split partials in
+// p.partial, on `stream`.
+int launch_head_and_merge(Slot& s, const rh::HeadParams& p, bool emit_logits, int grid, cudaStream_t stream) {
+    RH_CUDA(rh::launch_head(p, emit_logits, grid, stream));
+    s.launches++;
+    if (!emit_logits && p.n_splits > 1) {
+        RH_CUDA(rh::launch_merge(p.partial, p.n_splits, p.m, p.idx, p.prob, stream));
+        s.launches++;
+    }
+    return RH_OK;
+}
+
+// Enqueues the head (and the split merge) for rows [0, rows) of d_a on `stream`.
+int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per& pw, const float* d_a, int64_t rows,
+                 int32_t* d_idx, float* d_prob, float* d_logits, bool emit_logits, cudaStream_t stream,
+                 int64_t a_t = 0) {
+    if (rows <= 0) return RH_OK;
+    int grid;
+    rh::HeadParams p = head_params(ctx, w, s, pw, d_a, rows, a_t, d_idx, d_prob, d_logits, grid);
+    const bool split = !emit_logits && p.n_splits > 1;
+    if (split) {
         // The split scratch is the slot's: order this call after the previous merge that read
         // it (which may run on another caller stream), and let that merge finish before the
         // buffer is reallocated.
         if (!s.part_done) RH_CUDA(cudaEventCreateWithFlags(&s.part_done, cudaEventDisableTiming));
-        const size_t need = (size_t)n_splits * (size_t)rows * sizeof(float4);
+        const size_t need = (size_t)p.n_splits * (size_t)rows * sizeof(float4);
         if (need > s.partial.cap) RH_CUDA(cudaEventSynchronize(s.part_done));
         RH_CUDA(s.partial.ensure(need));
         RH_CUDA(cudaStreamWaitEvent(stream, s.part_done, 0));
         p.partial = static_cast<float4*>(s.partial.p);
     }
-    RH_CUDA(rh::launch_head(p, emit_logits, grid, stream));
-    s.launches++;
-    if (!emit_logits && n_splits > 1) {
-        RH_CUDA(rh::launch_merge(p.partial, n_splits, rows, d_idx, d_prob, stream));
-        s.launches++;
-        RH_CUDA(cudaEventRecord(s.part_done, stream));
-    }
+    if (int rc = launch_head_and_merge(s, p, emit_logits, grid, stream)) return rc;
+    if (split) RH_CUDA(cudaEventRecord(s.part_done, stream));
     return RH_OK;
 }
 
@@ -1302,43 +1321,18 @@ int rh_head_decode_device_noalloc(rh_ctx* ctx, const rh_weight* w, int slot, con
     float4* scratch = nullptr;
     if (int rc = noalloc_scratch(s.device, &scratch)) return rc;
 
-    int n_mblocks, n_splits, cps, grid;
-    plan(rows, w->g.n_chunks, s.sms, n_mblocks, n_splits, cps, grid);
-    if (n_splits > 1 && (int64_t)n_splits * rows > kNoAllocScratchEntries) {
+    int grid;
+    rh::HeadParams p = head_params(ctx, w, s, *pw, d_a, rows, 0, d_idx, d_prob, nullptr, grid);
+    if (p.n_splits > 1 && (int64_t)p.n_splits * rows > kNoAllocScratchEntries) {
         // fewer, longer class ranges so that splits x rows partial entries fit the array
         const int max_splits = (int)(kNoAllocScratchEntries / rows);
-        cps = max_splits <= 1 ? w->g.n_chunks : (w->g.n_chunks + max_splits - 1) / max_splits;
-        n_splits = (w->g.n_chunks + cps - 1) / cps;
-        grid = (int)std::min<long long>((long long)n_mblocks * n_splits, s.sms);
+        const int cps = max_splits <= 1 ? w->g.n_chunks : (w->g.n_chunks + max_splits - 1) / max_splits;
+        p.chunks_per_split = cps;
+        p.n_splits = (w->g.n_chunks + cps - 1) / cps;
+        grid = (int)std::min<long long>((long long)p.n_mblocks * p.n_splits, s.sms);
     }
-    rh::HeadParams p{};
-    p.a = d_a;
-    p.m = rows;
-    p.k = (int)w->k;
-    p.n = (int)w->n;
-    p.n_chunks = w->g.n_chunks;
-    p.hi_steps = w->g.hi_steps;
-    p.lo_steps = w->g.lo_steps;
-    p.merged_tail = w->g.merged;
-    p.btiles = pw->tiles;
-    p.colp = pw->colp;
-    p.ctab = pw->ctab;
-    p.poly_pairs = poly_pairs_setting();
-    p.n_mblocks = n_mblocks;
-    p.n_splits = n_splits;
-    p.chunks_per_split = cps;
-    p.idx = d_idx;
-    p.prob = d_prob;
-    p.partial = n_splits > 1 ? scratch : nullptr;
-    p.status = s.d_status;
-    p.timeout_ns = ctx->timeout_ns;
-    RH_CUDA(rh::launch_head(p, false, grid, (cudaStream_t)stream));
-    s.launches++;
-    if (n_splits > 1) {
-        RH_CUDA(rh::launch_merge(scratch, n_splits, rows, d_idx, d_prob, (cudaStream_t)stream));
-        s.launches++;
-    }
-    return RH_OK;
+    p.partial = p.n_splits > 1 ? scratch : nullptr;
+    return launch_head_and_merge(s, p, false, grid, (cudaStream_t)stream);
 }
 
 // ------------------------------------------------------ recognition preprocessing

@@ -1,7 +1,7 @@
-"""The benchmark's CPU-side contract: the reference arm (`bench.py --impl reference`, which
-the round-end driver runs beside ours) prints one JSON line with the fields it promises, and
-the helpers the GPU arm uses (workload shapes, sharding, the committed traffic figure)
-behave. Nothing here needs a GPU."""
+"""The benchmark's CPU-side contract: the reference arm (`bench.py --impl reference`, timed
+beside ours) prints one JSON line with the fields it promises, and the helpers the GPU arm
+uses (workload shapes, sharding, the recorded traffic figure) behave. Nothing here needs a
+GPU."""
 import json
 import os
 import subprocess
@@ -32,9 +32,12 @@ def test_reference_arm_prints_the_contract_line():
     assert "workload" in rec["config"]
 
 
-def test_reference_arm_for_the_fp32_head_reports_unavailable():
-    rec = _run("--impl", "reference", "--weights", "f32", "--steps", "1", "--warmup", "0")
-    assert rec["impl"] == "reference" and "unavailable" in rec
+def test_reference_arm_for_the_fp32_head():
+    """The FP32 head's CPU arm times matmul_transposed_b's blocked kernel restated."""
+    rec = _run("--impl", "reference", "--weights", "f32", "--steps", "1", "--warmup", "0",
+               "--cpu-sample-lines", "4")
+    assert rec["impl"] == "reference" and rec["value"] > 0 and rec["metric"].startswith("FP32")
+    assert rec["cpu_baseline"]["kind"] == "port"
 
 
 def test_bench_helpers():
@@ -48,8 +51,11 @@ def test_bench_helpers():
     assert bench.head_dims("tiny") == (80, 6906) and bench.head_dims("cfg2") == (120, 18710)
     w, b = bench.head_weights("tiny")
     assert w.shape == (6906, 80) and b.shape == (6906,)
-    t = bench.profiled_traffic()
-    assert t is None or t > 60_000_000  # DRAM bytes of one cfg2 launch from the committed ncu summary
+    t, src = bench.profiled_traffic("cfg2", "int8")
+    # DRAM bytes of one cfg2 launch, recorded for the current kernel sources (else None + why)
+    assert (t is None and src) or t > 60_000_000
+    assert len(bench.kernel_source_sha16()) == 16
+    assert bench.profiled_traffic("nonexistent", "int8")[0] is None
     assert np.all(np.diff(off) >= 0)
 
 

@@ -8,6 +8,8 @@ Bars (from the task's north star):
   * fused argmax: identical except where the oracle's top-2 logit gap is < 1e-5 (such
     near-ties are logged); max probability within 1e-5 relative where the argmax agrees.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -238,7 +240,8 @@ def test_fused_cfg1_ragged_lines(rh, ctx, oracle):
 
 
 def test_fused_cfg2_page_batch_subset(rh, ctx, oracle):
-    """cfg2's shapes with 96 of its 1024 lines (the oracle needs ~1 ms per row)."""
+    """cfg2's shapes with 96 of its 1024 lines, a quick first check; tests/test_gpu_full_size.py
+    checks every row of every config."""
     from rust_ppocrv6_b200 import workloads
 
     fused_case(rh, ctx, oracle, workloads.make(2, scale=96 / 1024), "cfg2/96")
@@ -698,23 +701,20 @@ def test_ctc_decode_from_fused_head(rh, ctx, oracle):
 # ------------------------------------------------------------ FP32 head
 
 
-def _oracle_f32_head(oracle, x, w_t, bias):
-    """matmul_transposed_b (exact product) -> softmax_inplace -> find_argmax, per timestep, with
-    the top-2 logit gap for the near-tie rule."""
-    logits = oracle.matmul_f32_transposed_b(x, w_t, bias)
-    probs = oracle.softmax_lastaxis(logits)
-    idx = np.empty(x.shape[0], np.int32)
-    prob = np.empty(x.shape[0], np.float32)
-    for r in range(x.shape[0]):
-        idx[r], prob[r] = oracle.find_argmax(probs[r])
-    top2 = np.sort(logits, axis=1)[:, -2:]
-    return logits, {"idx": idx, "prob": prob, "gap": (top2[:, 1] - top2[:, 0]).astype(np.float32)}
+def _oracle_f32_head(oracle, x, w_t, bias, line_offsets=None):
+    """The reference's FP32 head restated (matmul_transposed_b's register-blocked AVX2 kernel
+    -> softmax_inplace -> find_argmax) per timestep, with the top-2 logit gap for the
+    near-tie rule."""
+    off = np.array([0, x.shape[0]], np.int64) if line_offsets is None else line_offsets
+    ref = oracle.head_decode_f32(x, off, w_t, bias, threads=os.cpu_count() or 1, want_logits=True, want_gap=True)
+    return ref.pop("logits"), ref
 
 
 @pytest.mark.parametrize("n,k", [(18710, 120), (6906, 80), (1000, 64), (533, 123), (129, 17), (5, 8)])
 def test_fp32_head_logits_match_the_fp32_product(rh, ctx, oracle, n, k):
     """The engine's default head (quantize_rec_head = false): matmul_transposed_b with FP32
-    weights, against the exact product, for both fast layouts (K=120, K=80) and the generic ones."""
+    weights, against the reference's FP32 kernel restated (and the exact product), for both
+    fast layouts (K=120, K=80) and the generic ones."""
     rng = np.random.default_rng(41 + n + k)
     w = (0.05 * rng.standard_normal((n, k))).astype(np.float32)
     w[0] = 0.0                     # an all-zero class
@@ -725,14 +725,14 @@ def test_fp32_head_logits_match_the_fp32_product(rh, ctx, oracle, n, k):
     fw = rh.Fp32Weight.from_f32_transposed(w, ctx=ctx, bias=bias)
     x = rng.standard_normal((200, k), dtype=np.float32)
     got = rh.matmul_transposed_b(x, fw, bias)
-    ref = oracle.matmul_f32_transposed_b(x, w, bias)
     # any f32 dot product (the reference's FP32 kernel included) is off by up to ~1e-6 of the
     # sum of |terms|; with cancellation that exceeds 2e-6 of the result, so bound by the terms
     terms = np.abs(x).astype(np.float64) @ np.abs(w).astype(np.float64).T
-    err = np.abs(got.astype(np.float64) - ref)
-    assert np.all(err <= LOGIT_ABS_TOL + LOGIT_REL_TOL * terms), f"max err {err.max():.3g}"
-    plain = terms < 50.0  # ordinary rows also meet the plain logits bar
-    assert np.all(err[plain] <= LOGIT_ABS_TOL + LOGIT_REL_TOL * np.abs(ref[plain]))
+    for ref in (oracle.matmul_transposed_b(x, w, bias), oracle.matmul_f32_transposed_b(x, w, bias)):
+        err = np.abs(got.astype(np.float64) - ref)
+        assert np.all(err <= LOGIT_ABS_TOL + LOGIT_REL_TOL * terms), f"max err {err.max():.3g}"
+        plain = terms < 50.0  # ordinary rows also meet the plain logits bar
+        assert np.all(err[plain] <= LOGIT_ABS_TOL + LOGIT_REL_TOL * np.abs(ref[plain]))
     fw.free()
 
 
@@ -742,7 +742,7 @@ def test_fp32_head_fused_and_real_weights(rh, ctx, oracle):
     wl = workloads.make(1, scale=6 / 64)
     fw = rh.Fp32Weight.from_f32_transposed(wl.w_t, ctx=ctx, bias=wl.bias)
     idx, prob = rh.head_decode(wl.x, fw, line_offsets=wl.line_offsets)
-    _, ref = _oracle_f32_head(oracle, wl.x, wl.w_t, wl.bias)
+    _, ref = _oracle_f32_head(oracle, wl.x, wl.w_t, wl.bias, wl.line_offsets)
     assert_fused(idx, prob, ref, "fp32")
     # the collapse on the GPU works on the FP32 head too
     tokens, toff, scores = rh.head_decode_ctc(wl.x, fw, wl.line_offsets)
@@ -755,7 +755,7 @@ def test_fp32_head_fused_and_real_weights(rh, ctx, oracle):
     g = np.load(os.path.join(os.path.dirname(__file__), "golden", "real_head_slice.npz"))
     fw = rh.Fp32Weight.from_f32_transposed(g["w_t"], ctx=ctx, bias=g["bias"])
     x = np.random.default_rng(43).standard_normal((300, g["w_t"].shape[1]), dtype=np.float32)
-    assert_logits_close(rh.matmul_transposed_b(x, fw, g["bias"]), oracle.matmul_f32_transposed_b(x, g["w_t"], g["bias"]))
+    assert_logits_close(rh.matmul_transposed_b(x, fw, g["bias"]), oracle.matmul_transposed_b(x, g["w_t"], g["bias"]))
     idx, prob = rh.head_decode(x, fw)
     _, ref = _oracle_f32_head(oracle, x, g["w_t"], g["bias"])
     assert_fused(idx, prob, ref, "fp32-real")

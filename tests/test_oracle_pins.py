@@ -59,7 +59,7 @@ def test_quantized_matmul_handles_leading_batch_dims(oracle):
     a = sinpat(batch * k, 0.11, cos=True).reshape(batch, 1, k)
     got = oracle.matmul_quantized_b(a, q, s, None)
     assert got.shape == (batch, 1, n)
-    fp32 = oracle.matmul_f32_transposed_b(a, bt)
+    fp32 = oracle.matmul_transposed_b(a, bt)
     assert np.all(np.abs(got - fp32) <= 0.05 + 0.05 * np.abs(fp32))
 
 
@@ -81,7 +81,7 @@ def test_matmul_quantized_b_tracks_fp32_within_quantization_error(oracle):
     w = (np.cos(i.astype(np.float32) * np.float32(0.07)) * np.float32(0.5)
          + (i % 11).astype(np.float32) * np.float32(0.01)).astype(np.float32).reshape(n, k)
     q, s = oracle.pack(w)
-    fp32 = oracle.matmul_f32_transposed_b(a, w)
+    fp32 = oracle.matmul_transposed_b(a, w)
     int8 = oracle.matmul_quantized_b(a, q, s, None)
     max_abs = np.max(np.abs(fp32))
     tol = 1e-4 + 0.02 * np.abs(fp32) + 0.02 * max_abs
@@ -119,6 +119,94 @@ def test_colsplit_schedule_close_to_serial(oracle):
     for th in (1, 3, 7):
         cs = oracle.matmul_quantized_b_colsplit(a, q, s, b, threads=th)
         assert np.max(np.abs(cs - ser)) <= 1e-5
+
+
+# ---------------------------------------------- FP32 projection (matmul_transposed_b)
+
+
+def _ref_transposed_b(a, b_t):
+    """reference_transposed_b of src/ops/matmul.rs:1539-1550: the f64 product per row."""
+    return a.astype(np.float64) @ b_t.astype(np.float64).T
+
+
+def test_fp32_matmul_handles_leading_batch_dims(oracle):
+    """src/ops/matmul.rs:1559-1588 ([3, 1, K] input)."""
+    batch, k, n = 3, 8, 1024
+    bt = sinpat(n * k, 0.07).reshape(n, k)
+    a = sinpat(batch * k, 0.11, cos=True).reshape(batch, 1, k)
+    got = oracle.matmul_transposed_b(a, bt)
+    assert got.shape == (batch, 1, n)
+    assert np.all(np.abs(got.reshape(batch, n) - _ref_transposed_b(a.reshape(batch, k), bt)) < 1e-4)
+
+
+@pytest.mark.skipif("not __import__('oracle.oracle', fromlist=['x']).has_avx2()")
+@pytest.mark.parametrize("shape", [(3, 1, 8), (2, 3, 8), (4, 1, 16)])
+def test_fp32_matmul_identical_on_both_paths(oracle, shape):
+    """src/ops/matmul.rs:1590-1636: scalar and AVX2 paths agree and both match f64."""
+    batch, m, k = shape
+    n = 1024
+    bt = sinpat(n * k, 0.03, cos=True).reshape(n, k)
+    a = sinpat(batch * m * k, 0.05).reshape(shape)
+    scalar = oracle.matmul_transposed_b(a, bt, use_avx2=False)
+    wide = oracle.matmul_transposed_b(a, bt, use_avx2=True)
+    assert np.all(np.abs(wide - scalar) <= 1e-4 + 1e-4 * np.abs(scalar))
+    ref = _ref_transposed_b(a.reshape(-1, k), bt)
+    assert np.all(np.abs(scalar.reshape(-1, n) - ref) < 1e-4)
+
+
+def test_fp32_blocked_kernel_ragged_edges(oracle):
+    """src/ops/matmul.rs:1638-1671: rows 1..TILE_ROWS+2, column tails 0..3, with and without
+    a bias (which pins the column offset the tile reads it at)."""
+    k = 8
+    for n_tail in range(4):
+        n = 4 * 6 + n_tail
+        bt = sinpat(n * k, 0.031, cos=True).reshape(n, k)
+        for rows in range(1, 3 + 3):
+            a = sinpat(rows * k, 0.07).reshape(rows, k)
+            for bias in (None, np.full(n, 0.5, np.float32)):
+                got = oracle.matmul_transposed_b(a, bt, bias)
+                want = _ref_transposed_b(a, bt) + (0.5 if bias is not None else 0.0)
+                assert got.shape == (rows, n)
+                assert np.all(np.abs(got - want) < 1e-4), (n, rows, bias is not None)
+
+
+def test_fp32_matmul_argument_errors(oracle):
+    """src/ops/matmul.rs:1700-1721 and the inner-dimension check :531-536."""
+    a = np.arange(8, dtype=np.float32).reshape(1, 8)
+    bt = np.ones((16, 8), np.float32)
+    for n_bias in (0, 1, 15, 17):
+        with pytest.raises(ValueError):
+            oracle.matmul_transposed_b(a, bt, np.full(n_bias, 0.25, np.float32))
+    with pytest.raises(ValueError):
+        oracle.matmul_transposed_b(np.zeros((2, 7), np.float32), bt)
+
+
+@pytest.mark.skipif("not __import__('oracle.oracle', fromlist=['x']).has_avx2()")
+def test_fp32_head_shape_rows_and_fused_decode(oracle):
+    """The recognition head's shape (n = 18710: a tail of 2 columns through avx2_dot_product,
+    the rest through the blocked tile): within 1e-4 of the f64 product, each row's bits
+    independent of the row group of 3 it falls in, and the per-line fused decode equal to
+    projection -> softmax -> find_argmax."""
+    rng = np.random.default_rng(5)
+    n, k, m = 18710, 120, 7
+    bt = (0.05 * rng.standard_normal((n, k))).astype(np.float32)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = (0.01 * rng.standard_normal(n)).astype(np.float32)
+    got = oracle.matmul_transposed_b(a, bt, b)
+    ref = _ref_transposed_b(a, bt) + b
+    assert np.max(np.abs(got - ref)) < 1e-4
+    # rows are independent of their grouping: one row at a time gives the same bits
+    for r in range(m):
+        one = oracle.matmul_transposed_b(a[r:r + 1], bt, b)
+        assert np.array_equal(one.view(np.uint32), got[r:r + 1].view(np.uint32))
+    # per-line fused head over the FP32 projection = projection -> softmax -> argmax
+    off = np.array([0, 3, 7], np.int64)
+    h = oracle.head_decode_f32(a, off, bt, b, threads=2, want_logits=True, want_gap=True)
+    assert np.array_equal(h["logits"].view(np.uint32), got.view(np.uint32))
+    p = oracle.softmax_lastaxis(got)
+    for r in range(m):
+        i, v = oracle.find_argmax(p[r])
+        assert h["idx"][r] == i and h["prob"][r] == np.float32(v)
 
 
 # ------------------------------------------------------------- softmax
