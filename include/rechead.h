@@ -75,6 +75,17 @@ int rh_ctx_set_timeout_ms(rh_ctx *ctx, int timeout_ms);
 int rh_weight_pack(rh_ctx *ctx, const float *w_nk, int64_t n, int64_t k, const float *bias, int64_t bias_len,
                    rh_weight **out);
 
+/*
+ * rh_weight_pack with the weight kept in HBM as int8 (16 KB per 128 classes, q + 128 per byte,
+ * plus the f32 (scale, bias) table): 2.56 MB for the 18710 x 120 head, against 8.98 MB for the
+ * FP32 copy, the footprint cut of Model::quantize_matmul_weights that the reference asserts
+ * (src/engine/model.rs:2905-2920: at least 3.5x). The kernel expands each tile to fp16 in shared
+ * memory, which costs issue slots: decoded results are bit-identical to rh_weight_pack's, at
+ * lower throughput. Same arguments and errors as rh_weight_pack.
+ */
+int rh_weight_pack_compact(rh_ctx *ctx, const float *w_nk, int64_t n, int64_t k, const float *bias,
+                           int64_t bias_len, rh_weight **out);
+
 /* Replaces the folded bias (NULL: no bias). bias_len must equal n. The MatMul arm passes the
  * folded Add.204 bias on every call (src/engine/model.rs:1248-1252, :1261-1262). */
 int rh_weight_set_bias(rh_ctx *ctx, rh_weight *w, const float *bias, int64_t bias_len);
@@ -83,14 +94,26 @@ int rh_weight_set_bias(rh_ctx *ctx, rh_weight *w, const float *bias, int64_t bia
  * context device (src/ops/matmul.rs:1165-1171); either pointer may be NULL. */
 int rh_weight_export(rh_ctx *ctx, const rh_weight *w, int8_t *q, float *scales);
 
-/* Copies out the tensor-core image of the weight (n_chunks * 32768 bytes, n_chunks =
- * ceil(n/128)) and the per-class (scale, bias) table (n_chunks * 128 float pairs). */
-int rh_weight_export_image(rh_ctx *ctx, const rh_weight *w, uint8_t *tiles, float *colp);
+/* Copies out the device form of a quantised weight: its tiles (n_chunks = ceil(n/128) tiles of
+ * rh_weight_tile_bytes bytes) and its class table (n_chunks * 256 floats: per tile scale[128],
+ * then bias[128]; padded classes (0, -inf)). Either pointer may be NULL. Tile t holds classes
+ * 128 t .. 128 t + 127 (row r = class - 128 t) over K slots s < 128:
+ *  - rh_weight_pack: fp16 q at byte (s / 64) 16384 + 128 r + 16 (((s % 64) / 8) ^ (r % 8)) + 2 (s % 8)
+ *    (the tensor core's 128-byte-swizzled operand image);
+ *  - rh_weight_pack_compact: byte q + 128 at 16 ((8 (r / 8) + s / 16) 8 + r % 8) + s % 16.
+ * K slots >= k hold q = 0, except that when the last 16-slot step holds <= 8 values its upper 8
+ * slots repeat the lower 8. */
+int rh_weight_export_image(rh_ctx *ctx, const rh_weight *w, uint8_t *tiles, float *table);
+
+/* Bytes per 128-class tile of the packed weight on the device: 32768 (rh_weight_pack), 16384
+ * (rh_weight_pack_compact), 65536 (rh_weight_pack_f32); 0 for NULL. */
+int64_t rh_weight_tile_bytes(const rh_weight *w);
 
 int rh_weight_dims(const rh_weight *w, int64_t *n, int64_t *k);
 
-/* Device bytes held per device by the packed weight (Model::weight_footprint_bytes,
- * src/engine/model.rs:651-667, for the head). */
+/* Device bytes held per device by the packed weight: its tiles plus the (scale, bias) class
+ * table, nothing else (Model::weight_footprint_bytes, src/engine/model.rs:651-667, for the
+ * head). 18710 x 120 head: 2,558,976 compact, 4,967,424 fp16 image, 9,784,320 FP32. */
 int64_t rh_weight_device_bytes(const rh_weight *w);
 
 void rh_weight_free(rh_weight *w);

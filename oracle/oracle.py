@@ -54,13 +54,13 @@ def lib() -> ctypes.CDLL:
     L.oracle_ctc_collapse.argtypes = [_i32p, _f32p, _i64p, _i64, _i32p, _i64p, _f32p]
     L.oracle_ctc_collapse.restype = _i64
     L.oracle_head_decode.argtypes = [_f32p, _i64p, _i64, _i64, _i8p, _f32p, _i64, _vp, _i32p, _f32p, _vp, _vp,
-                                     _int, _int]
+                                     _vp, _int, _int]
     L.oracle_head_decode_one_line.argtypes = [_f32p, _i64, _i64, _i8p, _f32p, _i64, _vp, _i32p, _f32p, _f32p,
                                               _int, _int]
     L.oracle_matmul_f32_transposed_b.argtypes = [_f32p, _i64, _i64, _f32p, _i64, _vp, _f32p]
     L.oracle_matmul_transposed_b.argtypes = [_f32p, _i64, _i64, _f32p, _i64, _vp, _f32p, _int]
-    L.oracle_head_decode_f32.argtypes = [_f32p, _i64p, _i64, _i64, _f32p, _i64, _vp, _i32p, _f32p, _vp, _vp, _int,
-                                         _int]
+    L.oracle_head_decode_f32.argtypes = [_f32p, _i64p, _i64, _i64, _f32p, _i64, _vp, _i32p, _f32p, _vp, _vp, _vp,
+                                         _int, _int]
     L.oracle_exp_poly.argtypes = [ctypes.c_float]
     L.oracle_exp_poly.restype = ctypes.c_float
     _u32 = ctypes.c_uint32
@@ -187,7 +187,8 @@ def ctc_collapse(idx: np.ndarray, prob: np.ndarray, line_offsets: np.ndarray):
 def head_decode(a, line_offsets, q, scales, bias, threads=1, use_avx2=True, want_logits=False, want_gap=False):
     """The whole head per timestep row: MatMul.12 (+ folded bias) -> Softmax.2 -> argmax.
 
-    a [M,k] with lines at line_offsets; returns dict(idx int32[M], prob f32[M], logits?, gap?).
+    a [M,k] with lines at line_offsets; returns dict(idx int32[M], prob f32[M], logits?, and
+    with want_gap: gap = top-2 logit gap and lmax = largest logit, f32[M] each).
     """
     a = _c(a, np.float32)
     off = _c(line_offsets, np.int64)
@@ -197,14 +198,16 @@ def head_decode(a, line_offsets, q, scales, bias, threads=1, use_avx2=True, want
     prob = np.empty(m, np.float32)
     logits = np.empty((m, n), np.float32) if want_logits else None
     gap = np.empty(m, np.float32) if want_gap else None
+    lmax = np.empty(m, np.float32) if want_gap else None
     b = None if bias is None else _c(bias, np.float32)
     lib().oracle_head_decode(a, off, off.size - 1, k, _c(q, np.int8), _c(scales, np.float32), n, _ptr(b), idx,
-                             prob, _ptr(logits), _ptr(gap), int(threads), int(use_avx2))
+                             prob, _ptr(logits), _ptr(gap), _ptr(lmax), int(threads), int(use_avx2))
     out = {"idx": idx, "prob": prob}
     if want_logits:
         out["logits"] = logits
     if want_gap:
         out["gap"] = gap
+        out["lmax"] = lmax
     return out
 
 
@@ -263,14 +266,16 @@ def head_decode_f32(a, line_offsets, w_t, bias, threads=1, use_avx2=True, want_l
     prob = np.empty(m, np.float32)
     logits = np.empty((m, n), np.float32) if want_logits else None
     gap = np.empty(m, np.float32) if want_gap else None
+    lmax = np.empty(m, np.float32) if want_gap else None
     b = None if bias is None else _c(bias, np.float32)
     lib().oracle_head_decode_f32(a, off, off.size - 1, k, w_t, n, _ptr(b), idx, prob, _ptr(logits), _ptr(gap),
-                                 int(threads), int(use_avx2))
+                                 _ptr(lmax), int(threads), int(use_avx2))
     out = {"idx": idx, "prob": prob}
     if want_logits:
         out["logits"] = logits
     if want_gap:
         out["gap"] = gap
+        out["lmax"] = lmax
     return out
 
 

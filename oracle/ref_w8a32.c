@@ -560,12 +560,13 @@ int64_t oracle_ctc_collapse(const int32_t *idx, const float *prob, const int64_t
  * (src/engine/model.rs:1245-1272) -> matmul_quantized_b with the folded bias, the Softmax
  * arm (:1286-1302) -> softmax_inplace, then CtcDecoder's per-timestep find_argmax
  * (src/postprocess/ctc.rs:144-149). Emits (idx, prob) per timestep; optionally the raw
- * logits and the top-2 logit gap (max - second max) used to recognise near-ties.
+ * logits, the top-2 logit gap (max - second max) used to recognise near-ties and the row's
+ * largest logit.
  */
 typedef struct {
     const float *a; int64_t k, n; const int8_t *w; const float *s; const float *bias;
     const int64_t *offsets; int64_t n_units;
-    int32_t *idx; float *prob; float *logits_out; float *gap; int use_avx2;
+    int32_t *idx; float *prob; float *logits_out; float *gap; float *lmax; int use_avx2;
     atomic_long next;
 } head_job;
 
@@ -576,7 +577,7 @@ static void head_rows(head_job *j, int64_t r0, int64_t r1, float *row_buf) {
             oracle_cols_avx2(j->a + r * j->k, j->w, j->s, j->bias, lg, 0, j->n, j->k);
         else
             oracle_cols_scalar(j->a + r * j->k, j->w, j->s, j->bias, lg, 0, j->n, j->k);
-        if (j->gap) {
+        if (j->gap || j->lmax) {
             float m1 = -INFINITY, m2 = -INFINITY;
             for (int64_t c = 0; c < j->n; c++) {
                 float v = lg[c];
@@ -587,7 +588,8 @@ static void head_rows(head_job *j, int64_t r0, int64_t r1, float *row_buf) {
                     m2 = v;
                 }
             }
-            j->gap[r] = m1 - m2;
+            if (j->gap) j->gap[r] = m1 - m2;
+            if (j->lmax) j->lmax[r] = m1;
         }
         float *p = row_buf;
         if (j->use_avx2)
@@ -621,10 +623,10 @@ static void *head_worker(void *p) {
  */
 int oracle_head_decode(const float *a, const int64_t *line_offsets, int64_t n_lines, int64_t k, const int8_t *w,
                        const float *s, int64_t n, const float *bias, int32_t *idx, float *prob, float *logits_out,
-                       float *gap, int threads, int use_avx2) {
+                       float *gap, float *lmax, int threads, int use_avx2) {
     if (n_lines <= 0) return OR_OK;
     if (threads < 1) threads = 1;
-    head_job j = {a, k, n, w, s, bias, line_offsets, n_lines, idx, prob, logits_out, gap, use_avx2, 0};
+    head_job j = {a, k, n, w, s, bias, line_offsets, n_lines, idx, prob, logits_out, gap, lmax, use_avx2, 0};
     atomic_init(&j.next, 0);
     int nt = threads > 256 ? 256 : threads;
     if (nt > n_lines) nt = (int)n_lines;
@@ -834,7 +836,7 @@ void oracle_matmul_transposed_b(const float *a, int64_t rows, int64_t k, const f
 typedef struct {
     const float *a; int64_t k, n; const float *b_t; const float *bias;
     const int64_t *offsets; int64_t n_lines;
-    int32_t *idx; float *prob; float *logits_out; float *gap; int use_avx2;
+    int32_t *idx; float *prob; float *logits_out; float *gap; float *lmax; int use_avx2;
     atomic_long next;
 } f32_job;
 
@@ -854,7 +856,7 @@ static void *f32_worker(void *p) {
             for (int64_t rr = 0; rr < nr; rr++) {
                 const int64_t r = r0 + rr;
                 const float *row = lg + rr * j->n;
-                if (j->gap) {
+                if (j->gap || j->lmax) {
                     float m1 = -INFINITY, m2 = -INFINITY;
                     for (int64_t c = 0; c < j->n; c++) {
                         const float v = row[c];
@@ -865,7 +867,8 @@ static void *f32_worker(void *p) {
                             m2 = v;
                         }
                     }
-                    j->gap[r] = m1 - m2;
+                    if (j->gap) j->gap[r] = m1 - m2;
+                    if (j->lmax) j->lmax[r] = m1;
                 }
                 if (j->use_avx2)
                     oracle_softmax_row_avx2(row, prow, j->n);
@@ -890,10 +893,10 @@ static void *f32_worker(void *p) {
  */
 int oracle_head_decode_f32(const float *a, const int64_t *line_offsets, int64_t n_lines, int64_t k, const float *b_t,
                            int64_t n, const float *bias, int32_t *idx, float *prob, float *logits_out, float *gap,
-                           int threads, int use_avx2) {
+                           float *lmax, int threads, int use_avx2) {
     if (n_lines <= 0) return OR_OK;
     if (threads < 1) threads = 1;
-    f32_job j = {a, k, n, b_t, bias, line_offsets, n_lines, idx, prob, logits_out, gap, use_avx2, 0};
+    f32_job j = {a, k, n, b_t, bias, line_offsets, n_lines, idx, prob, logits_out, gap, lmax, use_avx2, 0};
     atomic_init(&j.next, 0);
     int nt = threads > 256 ? 256 : threads;
     if (nt > n_lines) nt = (int)n_lines;

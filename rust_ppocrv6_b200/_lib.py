@@ -36,6 +36,8 @@ SIGNATURES = {
     "rh_ctx_set_timeout_ms": (_c_int, [_vp, _c_int]),
     "rh_weight_pack": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _c_i64, ctypes.POINTER(_vp)]),
     "rh_weight_pack_f32": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _c_i64, ctypes.POINTER(_vp)]),
+    "rh_weight_pack_compact": (_c_int, [_vp, _vp, _c_i64, _c_i64, _vp, _c_i64, ctypes.POINTER(_vp)]),
+    "rh_weight_tile_bytes": (_c_i64, [_vp]),
     "rh_weight_set_bias": (_c_int, [_vp, _vp, _vp, _c_i64]),
     "rh_weight_export": (_c_int, [_vp, _vp, _vp, _vp]),
     "rh_weight_export_image": (_c_int, [_vp, _vp, _vp, _vp]),

@@ -9,8 +9,27 @@ namespace rh {
 constexpr int kBlockM = 128;                  // timestep rows per work unit (one TMEM lane each)
 constexpr int kBlockN = 128;                  // classes per weight tile / accumulator
 constexpr int kPadK = 128;                    // K extent of a weight tile (K <= 128 supported)
-constexpr int kTileBytes = kBlockN * kPadK * 2;  // one fp16 weight tile: 32 KB
-constexpr int kStages = 4;                    // weight-tile ring depth in shared memory
+constexpr int kTileBytes = kBlockN * kPadK * 2;  // one fp16 weight tile (the MMA's B operand): 32 KB
+constexpr int kTile8Bytes = kBlockN * kPadK;  // one int8 weight tile as stored in HBM: 16 KB
+constexpr int kCtabFloats = 2 * kBlockN;      // class table per tile: scale[128] then bias[128]
+// Shared-memory weight ring (128 KB), by the form of the weight in HBM:
+//  - fp16 image (rh_weight_pack): 4 stages of 32 KB, each filled by one bulk copy;
+//  - int8 tiles (rh_weight_pack_compact): 3 fp16 stages filled by the expander warps from 2
+//    int8 landing slots of 16 KB;
+//  - FP32 hi/lo images (rh_weight_pack_f32): 2 stages of 64 KB.
+constexpr int kStagesImage = 4;
+constexpr int kStages8 = 3;
+constexpr int kI8Slots = 2;
+constexpr int kStagesDual = 2;
+
+// Byte offset of class row r (0..127 within its tile) and K slot s (0..127) in an int8 tile:
+// 16-byte chunks of 16 K slots, ordered [row group r/8][K chunk s/16][row r%8]. The expander
+// warps read the tile as consecutive 16-byte chunks (conflict-free shared-memory loads) and
+// each 8-lane phase writes 8 rows of one K chunk, whose swizzled fp16 positions are distinct
+// (conflict-free stores).
+__host__ __device__ constexpr uint32_t image8_offset(int r, int s) {
+    return ((((uint32_t)(r >> 3) * 8u + (uint32_t)(s >> 4)) * 8u + (uint32_t)(r & 7)) << 4) + (uint32_t)(s & 15);
+}
 constexpr int kEpiGroups = 6;                 // epilogue warp groups (4 warps each)
 constexpr int kHeadThreads = 32 * (8 + 4 * kEpiGroups);  // 32 warps, see head_kernel
 
@@ -38,10 +57,12 @@ struct HeadParams {
     int hi_steps;              // MMA K-steps of the high fp16 part of A
     int lo_steps;              // MMA K-steps of the low fp16 part of A
     int merged_tail;           // 1: hi step hi_steps-1 also carries lo's last 8 K values
-    const uint8_t* btiles;     // n_chunks tiles of 32 KB (dual: 64 KB = hi then lo image), smem image order
+    const uint8_t* btiles;     // n_chunks tiles: fp16 image of 32 KB (shared-memory image order), or
+                               // (expand) int8 of 16 KB (expansion order, q + 128), or (dual) fp16
+                               // hi then lo image, 64 KB
     int dual;                  // FP32 weights: each tile holds fp16 hi and lo parts (A_hi.W_lo added)
-    const float2* colp;        // n_chunks * 128 (scale, bias); padded columns (0, -inf)
-    const float* ctab;         // n_chunks * 256: per tile c[128] = scale*log2(e), e[128] = bias*log2(e)
+    int expand;                // int8 tiles, expanded to fp16 in shared memory by warps 4-7
+    const float* ctab;         // n_chunks * 256: per tile scale[128] then bias[128]; padded classes (0, -inf)
     int n_mblocks;             // ceil(m / 128)
     int n_splits;              // class-range splits per row block
     int chunks_per_split;
@@ -64,11 +85,9 @@ struct PackParams {
     int merged_tail;
     int tail_step;             // index of the last hi K-step (ceil(k/16) - 1)
     int f32;                   // 1: FP32 weights (no int8): per-class power-of-two scale, fp16 hi + lo images
-    int8_t* q;                 // [n][k] canonical int8 (QuantizedWeight::data); unused when f32
-    float* scales;             // [n]; unused when f32
-    uint8_t* btiles;           // n_pad/128 tiles of 32 KB (f32: 64 KB, hi image then lo image)
-    float2* colp;              // [n_pad]
-    float* ctab;               // [n_pad / 128][256]
+    int compact;               // quantised only: 1 = int8 tiles (16 KB), 0 = fp16 image tiles (32 KB)
+    uint8_t* btiles;           // n_pad/128 tiles (f32: 64 KB, hi image then lo image)
+    float* ctab;               // [n_pad / 128][256] scale then bias per tile
 };
 
 // Batched recognition preprocessing (recpre_kernels.cu): RecPreprocess::process of each crop

@@ -155,27 +155,29 @@ struct rh_ctx {
 
 struct rh_weight {
     int64_t n = 0, k = 0;
-    bool f32 = false;  // FP32 head (rh_weight_pack_f32): hi/lo fp16 images, no int8
+    bool f32 = false;      // FP32 head (rh_weight_pack_f32): hi/lo fp16 images, no int8
+    bool compact = false;  // quantised, int8 tiles (rh_weight_pack_compact) instead of the fp16 image
     Geometry g{};
+    // Per device: the weight tiles (quantised: the fp16 image of the MMA operand, 32 KB per 128
+    // classes, or compact int8, 16 KB per 128 classes in the order the kernel expands them;
+    // FP32: fp16 hi and lo images, 64 KB per 128 classes) and the class table (scale[128] then
+    // bias[128] per tile). Nothing else stays on the device.
     struct Per {
         int device = 0;
-        int8_t* q = nullptr;
-        float* scales = nullptr;
         uint8_t* tiles = nullptr;
-        float2* colp = nullptr;
         float* ctab = nullptr;
     };
     std::vector<Per> per;
-    std::vector<float> host_scales;  // per-class scale (int8 scale, or 2^-sh for FP32), to rebuild the bias table
+    std::vector<float> host_scales;  // per-class scale (int8 scale, or 2^-sh for FP32), to rebuild the table
+    size_t tile_bytes() const {
+        return f32 ? 2u * rh::kTileBytes : compact ? (size_t)rh::kTile8Bytes : (size_t)rh::kTileBytes;
+    }
     // Frees every device copy, also for a weight whose packing failed part-way.
     ~rh_weight() {
         for (auto& p : per) {
             cudaSetDevice(p.device);
             cudaDeviceSynchronize();
-            cudaFree(p.q);
-            cudaFree(p.scales);
             cudaFree(p.tiles);
-            cudaFree(p.colp);
             cudaFree(p.ctab);
         }
     }
@@ -207,7 +209,7 @@ rh::HeadParams head_params(rh_ctx* ctx, const rh_weight* w, const Slot& s, const
     p.merged_tail = w->g.merged;
     p.btiles = pw.tiles;
     p.dual = w->f32 ? 1 : 0;
-    p.colp = pw.colp;
+    p.expand = w->compact ? 1 : 0;
     p.ctab = pw.ctab;
     p.poly_pairs = poly_pairs_setting();
     p.n_mblocks = n_mblocks;
@@ -377,21 +379,14 @@ int run_ctc_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, c
     return RH_OK;
 }
 
-int upload_colp(rh_ctx* ctx, rh_weight* w, const float* bias) {
+// Rewrites the class table (scale, bias per class; padded classes (0, -inf)) on every device.
+int upload_table(rh_ctx* ctx, rh_weight* w, const float* bias) {
     const int n_pad = w->g.n_chunks * rh::kBlockN;
-    std::vector<float2> colp(n_pad);
-    for (int j = 0; j < n_pad; ++j) {
-        if (j < w->n)
-            colp[j] = make_float2(w->host_scales[j], bias ? bias[j] : 0.0f);
-        else
-            colp[j] = make_float2(0.0f, -INFINITY);
-    }
-    const float kLog2e = 1.4426950408889634f;
-    std::vector<float> ctab((size_t)n_pad * 2);
+    std::vector<float> ctab((size_t)w->g.n_chunks * rh::kCtabFloats);
     for (int j = 0; j < n_pad; ++j) {
         const int t = j / rh::kBlockN, r = j % rh::kBlockN;
-        ctab[(size_t)t * 256 + r] = j < w->n ? w->host_scales[j] * kLog2e : 0.0f;
-        ctab[(size_t)t * 256 + 128 + r] = j < w->n ? (bias ? bias[j] : 0.0f) * kLog2e : -INFINITY;
+        ctab[(size_t)t * rh::kCtabFloats + r] = j < w->n ? w->host_scales[j] : 0.0f;
+        ctab[(size_t)t * rh::kCtabFloats + rh::kBlockN + r] = j < w->n ? (bias ? bias[j] : 0.0f) : -INFINITY;
     }
     for (auto& p : w->per) {
         Slot* slot = nullptr;
@@ -400,8 +395,6 @@ int upload_colp(rh_ctx* ctx, rh_weight* w, const float* bias) {
         if (!slot) return fail(RH_ERR_INVALID_ARG, "weight device is not in this context");
         RH_CUDA(cudaSetDevice(p.device));
         // ordered after every kernel already queued on the slot stream that reads the table
-        RH_CUDA(cudaMemcpyAsync(p.colp, colp.data(), colp.size() * sizeof(float2), cudaMemcpyHostToDevice,
-                                slot->stream));
         RH_CUDA(cudaMemcpyAsync(p.ctab, ctab.data(), ctab.size() * sizeof(float), cudaMemcpyHostToDevice,
                                 slot->stream));
         RH_CUDA(cudaStreamSynchronize(slot->stream));
@@ -844,7 +837,7 @@ int rh_ctx_set_timeout_ms(rh_ctx* ctx, int timeout_ms) {
 
 namespace {
 int pack_weight(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len, bool f32,
-                rh_weight** out) {
+                bool compact, rh_weight** out) {
     if (int rc = check_ctx(ctx)) return rc;
     if (!out || !w_nk) return fail(RH_ERR_INVALID_ARG, "null weight or output pointer");
     *out = nullptr;
@@ -859,6 +852,7 @@ int pack_weight(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const floa
     w->n = n;
     w->k = k;
     w->f32 = f32;
+    w->compact = compact && !f32;
     w->g = geometry(n, k);
     const int n_pad = w->g.n_chunks * rh::kBlockN;
     for (auto& sp : ctx->slots) {
@@ -867,13 +861,8 @@ int pack_weight(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const floa
         RH_CUDA(cudaSetDevice(s.device));
         rh_weight::Per p;
         p.device = s.device;
-        if (!f32) {
-            RH_CUDA(cudaMalloc(&p.q, (size_t)n * (size_t)k));
-            RH_CUDA(cudaMalloc(&p.scales, (size_t)n * sizeof(float)));
-        }
-        RH_CUDA(cudaMalloc(&p.tiles, (size_t)w->g.n_chunks * rh::kTileBytes * (f32 ? 2 : 1)));
-        RH_CUDA(cudaMalloc(&p.colp, (size_t)n_pad * sizeof(float2)));
-        RH_CUDA(cudaMalloc(&p.ctab, (size_t)n_pad * 2 * sizeof(float)));
+        RH_CUDA(cudaMalloc(&p.tiles, (size_t)w->g.n_chunks * w->tile_bytes()));
+        RH_CUDA(cudaMalloc(&p.ctab, (size_t)w->g.n_chunks * rh::kCtabFloats * sizeof(float)));
         w->per.push_back(p);
         DevBuf tw, tb;  // temporaries, freed on every path
         RH_CUDA(tw.ensure((size_t)n * (size_t)k * sizeof(float)));
@@ -896,21 +885,20 @@ int pack_weight(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const floa
         pp.merged_tail = w->g.merged;
         pp.tail_step = w->g.tail_step;
         pp.f32 = f32 ? 1 : 0;
-        pp.q = p.q;
-        pp.scales = p.scales;
+        pp.compact = w->compact ? 1 : 0;
         pp.btiles = p.tiles;
-        pp.colp = p.colp;
         pp.ctab = p.ctab;
         RH_CUDA(rh::launch_pack(pp, s.stream));
         s.launches++;
         RH_CUDA(cudaStreamSynchronize(s.stream));
-        if (w->host_scales.empty()) {  // the per-class scale is the .x of the epilogue table
-            std::vector<float2> colp((size_t)n);
-            RH_CUDA(cudaMemcpyAsync(colp.data(), p.colp, (size_t)n * sizeof(float2), cudaMemcpyDeviceToHost,
+        if (w->host_scales.empty()) {  // the per-class scales, read back from the class table
+            std::vector<float> ctab((size_t)w->g.n_chunks * rh::kCtabFloats);
+            RH_CUDA(cudaMemcpyAsync(ctab.data(), p.ctab, ctab.size() * sizeof(float), cudaMemcpyDeviceToHost,
                                     s.stream));
             RH_CUDA(cudaStreamSynchronize(s.stream));
             w->host_scales.resize((size_t)n);
-            for (int64_t j = 0; j < n; ++j) w->host_scales[(size_t)j] = colp[(size_t)j].x;
+            for (int64_t j = 0; j < n; ++j)
+                w->host_scales[(size_t)j] = ctab[(size_t)(j / rh::kBlockN) * rh::kCtabFloats + (size_t)(j % rh::kBlockN)];
         }
     }
     *out = w.release();
@@ -920,12 +908,17 @@ int pack_weight(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const floa
 
 int rh_weight_pack(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len,
                    rh_weight** out) {
-    return pack_weight(ctx, w_nk, n, k, bias, bias_len, false, out);
+    return pack_weight(ctx, w_nk, n, k, bias, bias_len, false, false, out);
+}
+
+int rh_weight_pack_compact(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len,
+                           rh_weight** out) {
+    return pack_weight(ctx, w_nk, n, k, bias, bias_len, false, true, out);
 }
 
 int rh_weight_pack_f32(rh_ctx* ctx, const float* w_nk, int64_t n, int64_t k, const float* bias, int64_t bias_len,
                        rh_weight** out) {
-    return pack_weight(ctx, w_nk, n, k, bias, bias_len, true, out);
+    return pack_weight(ctx, w_nk, n, k, bias, bias_len, true, false, out);
 }
 
 int rh_weight_set_bias(rh_ctx* ctx, rh_weight* w, const float* bias, int64_t bias_len) {
@@ -935,7 +928,7 @@ int rh_weight_set_bias(rh_ctx* ctx, rh_weight* w, const float* bias, int64_t bia
         return fail(RH_ERR_INVALID_ARG,
                     "bias has " + std::to_string(bias_len) + " elements but n is " + std::to_string(w->n));
     for (auto& s : ctx->slots) s->mu.lock();
-    int rc = upload_colp(ctx, w, bias);
+    int rc = upload_table(ctx, w, bias);
     for (auto& s : ctx->slots) s->mu.unlock();
     return rc;
 }
@@ -947,21 +940,43 @@ int rh_weight_export(rh_ctx* ctx, const rh_weight* w, int8_t* q, float* scales) 
     const auto& p = w->per[0];
     RH_CUDA(cudaSetDevice(p.device));
     RH_CUDA(cudaDeviceSynchronize());
-    if (q) RH_CUDA(cudaMemcpy(q, p.q, (size_t)w->n * (size_t)w->k, cudaMemcpyDeviceToHost));
-    if (scales) RH_CUDA(cudaMemcpy(scales, p.scales, (size_t)w->n * sizeof(float), cudaMemcpyDeviceToHost));
+    if (q) {  // QuantizedWeight::data read back from the tiles (fp16 image, or int8 stored as q + 128)
+        std::vector<uint8_t> img((size_t)w->g.n_chunks * w->tile_bytes());
+        RH_CUDA(cudaMemcpy(img.data(), p.tiles, img.size(), cudaMemcpyDeviceToHost));
+        for (int64_t j = 0; j < w->n; ++j) {
+            const uint8_t* tile = img.data() + (size_t)(j / rh::kBlockN) * w->tile_bytes();
+            const int r = (int)(j % rh::kBlockN);
+            for (int64_t s = 0; s < w->k; ++s) {
+                int v;
+                if (w->compact) {
+                    v = (int)tile[rh::image8_offset(r, (int)s)] - 128;
+                } else {  // integer-valued fp16 (|q| <= 127): sign, exponent and 10-bit fraction
+                    const uint32_t off = (uint32_t)(s >> 6) * 16384u + (uint32_t)r * 128u +
+                                         (uint32_t)((((s & 63) >> 3) ^ (r & 7)) << 4) + (uint32_t)(s & 7) * 2u;
+                    const uint16_t h = (uint16_t)(tile[off] | (tile[off + 1] << 8));
+                    const int e = (h >> 10) & 31;
+                    const int mag = e == 0 ? 0 : (int)(((h & 1023) | 1024) >> (25 - e));
+                    v = (h & 0x8000) ? -mag : mag;
+                }
+                q[(size_t)j * (size_t)w->k + (size_t)s] = (int8_t)v;
+            }
+        }
+    }
+    if (scales) std::memcpy(scales, w->host_scales.data(), (size_t)w->n * sizeof(float));
     return RH_OK;
 }
 
-int rh_weight_export_image(rh_ctx* ctx, const rh_weight* w, uint8_t* tiles, float* colp) {
+int rh_weight_export_image(rh_ctx* ctx, const rh_weight* w, uint8_t* tiles, float* table) {
     if (int rc = check_ctx(ctx)) return rc;
     if (!w || w->per.empty()) return fail(RH_ERR_INVALID_ARG, "null weight");
     if (w->f32) return fail(RH_ERR_INVALID_ARG, "the image of an FP32 weight is not exported");
     const auto& p = w->per[0];
     RH_CUDA(cudaSetDevice(p.device));
     RH_CUDA(cudaDeviceSynchronize());
-    if (tiles) RH_CUDA(cudaMemcpy(tiles, p.tiles, (size_t)w->g.n_chunks * rh::kTileBytes, cudaMemcpyDeviceToHost));
-    if (colp)
-        RH_CUDA(cudaMemcpy(colp, p.colp, (size_t)w->g.n_chunks * rh::kBlockN * sizeof(float2), cudaMemcpyDeviceToHost));
+    if (tiles) RH_CUDA(cudaMemcpy(tiles, p.tiles, (size_t)w->g.n_chunks * w->tile_bytes(), cudaMemcpyDeviceToHost));
+    if (table)
+        RH_CUDA(cudaMemcpy(table, p.ctab, (size_t)w->g.n_chunks * rh::kCtabFloats * sizeof(float),
+                           cudaMemcpyDeviceToHost));
     return RH_OK;
 }
 
@@ -972,10 +987,11 @@ int rh_weight_dims(const rh_weight* w, int64_t* n, int64_t* k) {
     return RH_OK;
 }
 
+int64_t rh_weight_tile_bytes(const rh_weight* w) { return w ? (int64_t)w->tile_bytes() : 0; }
+
 int64_t rh_weight_device_bytes(const rh_weight* w) {
     if (!w) return 0;
-    if (w->f32) return (int64_t)w->g.n_chunks * (2 * rh::kTileBytes + rh::kBlockN * 16);
-    return w->n * w->k + w->n * 4 + (int64_t)w->g.n_chunks * (rh::kTileBytes + rh::kBlockN * 16);
+    return (int64_t)w->g.n_chunks * ((int64_t)w->tile_bytes() + rh::kCtabFloats * (int64_t)sizeof(float));
 }
 
 void rh_weight_free(rh_weight* w) {

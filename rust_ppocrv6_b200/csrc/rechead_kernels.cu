@@ -32,28 +32,41 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 // ---------------------------------------------------------------- shared memory map
 // (offsets from the 1024-byte aligned base)
-constexpr uint32_t kOffB = 0;                                   // kStages weight tiles
-constexpr uint32_t kOffBars = kStages * kTileBytes;             // mbarriers (48 x 8 B)
+// Weight ring (128 KB): fp16 image weights kStagesImage stages of 32 KB (the MMA's B operand);
+// int8 tiles kStages8 fp16 stages at [0, 96 KB), then kI8Slots int8 landing slots of 16 KB;
+// FP32 weights kStagesDual stages of 64 KB (hi image, then lo image).
+constexpr uint32_t kOffB = 0;
+constexpr uint32_t kOffI8 = kStages8 * kTileBytes;
+constexpr uint32_t kWeightRegion = kOffI8 + kI8Slots * kTile8Bytes;
+static_assert(kWeightRegion >= (uint32_t)kStagesDual * 2u * kTileBytes &&
+                  kWeightRegion >= (uint32_t)kStagesImage * kTileBytes,
+              "every form's stages fit the weight ring");
+constexpr uint32_t kOffBars = kWeightRegion;                    // mbarriers (48 x 8 B)
 constexpr uint32_t kOffMisc = kOffBars + 48 * 8;                // [0] TMEM base, [1] abort flag
 constexpr uint32_t kOffRho = kOffMisc + 32;                     // [4][128] f32 row de-scale
 constexpr uint32_t kOffQFlag = kOffRho + 4 * 128 * 4;           // [4][4] u32 "quadrant needs de-scale"
 constexpr uint32_t kOffMerge = kOffQFlag + 16 * 4;              // [2][kEpiGroups-1][128] float4
 constexpr uint32_t kOffCtab = kOffMerge + 2 * (kEpiGroups - 1) * 128 * 16;  // [4 slots][256] f32 class table
 constexpr uint32_t kCtabSlots = 4;
-constexpr uint32_t kCtabBytes = 256 * 4;
+constexpr uint32_t kCtabBytes = kCtabFloats * 4;
 constexpr uint32_t kOffRowMax = kOffCtab + kCtabSlots * kCtabBytes;  // [128] u64 (unit tag, ordered max)
 constexpr uint32_t kOffAStage = kOffRowMax + 128 * 8;           // [128][k] f32 feature rows of a unit
 constexpr uint32_t kAStageBytes = kBlockM * kPadK * 4;
 constexpr uint32_t kSmemUsed = kOffAStage + kAStageBytes;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;               // + alignment slack
-static_assert(kOffCtab % 16 == 0 && kOffAStage % 16 == 0, "bulk-copy destination alignment");
+static_assert(kOffCtab % 16 == 0 && kOffAStage % 16 == 0 && kOffI8 % 1024 == 0, "bulk-copy destination alignment");
 static_assert(kSmemUsed + 1024 <= 227 * 1024, "shared memory per CTA");
 
 // mbarrier indices
-constexpr int kBarBFull = 0;                     // [kStages] weight tile landed
-constexpr int kBarBEmpty = kBarBFull + kStages;  // [kStages] MMAs reading the tile done
+constexpr int kMaxStages = kStagesImage;
+static_assert(kStagesImage >= kStages8 && kStagesImage >= kStagesDual, "stage barriers");
+constexpr int kExpanderWarps = 4;                // warps 4-7 (int8 -> fp16 stage expansion), one arrival each
+constexpr int kBarBFull = 0;                     // [kMaxStages] fp16 stage ready for the MMA
+constexpr int kBarBEmpty = kBarBFull + kMaxStages;  // [kMaxStages] MMAs reading the stage done
+constexpr int kBarI8Full = kBarBEmpty + kMaxStages;  // [kI8Slots] int8 tile landed
+constexpr int kBarI8Empty = kBarI8Full + kI8Slots;   // [kI8Slots] expanders done reading it
 constexpr int kAccBufs = 3;                      // accumulator buffers in TMEM
-constexpr int kBarAFull = kBarBEmpty + kStages;  // A operand of the unit written to TMEM
+constexpr int kBarAFull = kBarI8Empty + kI8Slots;  // A operand of the unit written to TMEM
 constexpr int kBarAEmpty = kBarAFull + 1;        // MMAs of the unit done with A
 constexpr int kBarAccFull = kBarAEmpty + 1;      // [kAccBufs] accumulator ready
 constexpr int kBarAccEmpty = kBarAccFull + kAccBufs;  // [kAccBufs] accumulator drained (four quarters loaded)
@@ -61,9 +74,10 @@ constexpr int kBarRhoFull = kBarAccEmpty + kAccBufs;  // [4] per-unit row de-sca
 constexpr int kBarMFull = kBarRhoFull + 4;       // [2] groups 1.. partials staged for the merge
 constexpr int kBarMEmpty = kBarMFull + 2;        // [2] group 0 consumed them
 constexpr int kBarMmaDone = kBarMEmpty + 2;      // all MMAs retired (teardown)
-constexpr int kBarCtabFull = kBarMmaDone + 1;    // [4] class table of a tile landed
+constexpr int kBarCtabFull = kBarMmaDone + 1;    // [4] class table of a tile in log2 units
 constexpr int kBarCtabEmpty = kBarCtabFull + 4;  // [4] all epilogue groups are done with it
-constexpr int kBarStageFull = kBarCtabEmpty + 4;  // f32 feature rows of the next unit landed
+constexpr int kBarCtabRaw = kBarCtabEmpty + 4;   // [4] (scale, bias) of a tile landed
+constexpr int kBarStageFull = kBarCtabRaw + 4;   // f32 feature rows of the next unit landed
 constexpr int kBarStageRead = kBarStageFull + 1;  // converters done reading the staged rows
 constexpr int kNumBars = kBarStageRead + 1;
 static_assert(kNumBars <= 48, "barrier area");
@@ -173,6 +187,16 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
     const uint32_t bx = __float_as_uint(p.x) + (__float_as_uint(r.x) << 23);
     const uint32_t by = __float_as_uint(p.y) + (__float_as_uint(r.y) << 23);
     return make_float2(__uint_as_float(bx), __uint_as_float(by));
+}
+
+// Two int8 weights stored as bytes b = q + 128 (selected from `w` by `sel`, a byte-permute
+// selector placing them in bytes 0 and 2) -> two fp16 values q: 0x64 above each byte gives
+// fp16 1024 + b, and subtracting 1152 leaves q exactly (all integers here are exact in fp16).
+__device__ __forceinline__ uint32_t q8_to_f16x2(uint32_t w, uint32_t sel) {
+    uint32_t h;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(h) : "r"(w), "r"(0x64646464u), "r"(sel));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(h) : "r"(0x64806480u));  // 0x6480 = fp16 1152
+    return h;
 }
 
 // Order-preserving map of a (non-NaN) f32 onto u32: a < b  <=>  ord(a) < ord(b).
@@ -330,15 +354,17 @@ __device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, ui
     }
 }
 
+// Logits of 32 columns: dot * scale + bias; `cp` points at the columns' scales in the
+// weight's class table, their biases sit 128 floats further.
 template <bool SCALED>
-__device__ __forceinline__ void logits_quarter(const uint32_t* v, const float2* __restrict__ cp, int col0,
+__device__ __forceinline__ void logits_quarter(const uint32_t* v, const float* __restrict__ cp, int col0,
                                                float rho, float* __restrict__ out_row, int n) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const float2 sb = __ldg(cp + i);
+        const float sc = __ldg(cp + i), bi = __ldg(cp + 128 + i);
         float x = __uint_as_float(v[i]);
         if (SCALED) x *= rho;
-        if (col0 + i < n) out_row[col0 + i] = fmaf(x, sb.x, sb.y);
+        if (col0 + i < n) out_row[col0 + i] = fmaf(x, sc, bi);
     }
 }
 
@@ -359,6 +385,12 @@ __device__ __forceinline__ void combine(float& m0, float& s0, int& i0, float m1,
 
 // ------------------------------------------------------------------------- pack
 // One warp per (padded) class row. Lane l holds K values l, l+32, l+64, l+96.
+// Writes the class table (scale, bias) and the tiles, in one of two forms:
+//  - fp16 image (the MMA's B operand as it sits in shared memory, one bulk copy per tile);
+//  - int8 (compact): q + 128 as a byte (so the expander can build fp16(1024 + byte) by a byte
+//    permute and subtract 1152), at image8_offset(row, K slot).
+// K slots >= k hold q = 0, and with a merged tail the last hi step's upper 8 slots repeat its
+// lower 8 (the low fp16 part of A rides there).
 __global__ void __launch_bounds__(256) pack_kernel(const PackParams p) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -387,19 +419,34 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackParams p) {
         else
             qi = (int)fminf(fmaxf(v, -127.0f), 127.0f);
         q[i] = real ? qi : 0;
-        const int kk = lane + 32 * i;
-        if (real && kk < p.k) p.q[(size_t)j * p.k + kk] = (int8_t)qi;
     }
     const int tile = j >> 7, r = j & 127;
-    if (real && lane == 0) p.scales[j] = scale;
     if (lane == 0) {
         const float b = (real && p.bias) ? p.bias[j] : 0.0f;
-        p.colp[j] = real ? make_float2(scale, b) : make_float2(0.0f, -CUDART_INF_F);
-        p.ctab[(size_t)tile * 256 + r] = real ? scale * kLog2e : 0.0f;
-        p.ctab[(size_t)tile * 256 + 128 + r] = real ? b * kLog2e : -CUDART_INF_F;
+        p.ctab[(size_t)tile * kCtabFloats + r] = real ? scale : 0.0f;
+        p.ctab[(size_t)tile * kCtabFloats + kBlockN + r] = real ? b : -CUDART_INF_F;
     }
-
-    // tensor-core image: tile j/128, row r = j%128, K slot s -> byte offset
+    if (p.compact) {
+        // int8 tiles: lane l writes K slots 4l..4l+3 (one 32-bit word of one 16-byte chunk)
+        uint32_t word = 0u;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int s = lane * 4 + t;  // K slot 0..127
+            int src = s;
+            if (p.merged_tail && s >= 16 * p.tail_step + 8 && s < 16 * p.tail_step + 16) src = s - 8;
+            const bool ok = src < p.k;
+            const int from = src & 31, reg = src >> 5;
+            const int v0 = __shfl_sync(0xffffffffu, q[0], from);
+            const int v1 = __shfl_sync(0xffffffffu, q[1], from);
+            const int v2 = __shfl_sync(0xffffffffu, q[2], from);
+            const int v3 = __shfl_sync(0xffffffffu, q[3], from);
+            const int val = ok ? (reg == 0 ? v0 : reg == 1 ? v1 : reg == 2 ? v2 : v3) : 0;
+            word |= (uint32_t)(val + 128) << (8 * t);
+        }
+        *reinterpret_cast<uint32_t*>(p.btiles + (size_t)tile * kTile8Bytes + image8_offset(r, lane * 4)) = word;
+        return;
+    }
+    // fp16 image: tile j/128, row r = j%128, K slot s -> byte offset
     // (s/64)*16384 + r*128 + (((s%64)/8) ^ (r%8))*16 + (s%8)*2
     uint8_t* img = p.btiles + (size_t)tile * kTileBytes;
 #pragma unroll
@@ -455,9 +502,8 @@ __global__ void __launch_bounds__(256) pack_f32_kernel(const PackParams p) {
     const int tile = j >> 7, r = j & 127;
     if (lane == 0) {
         const float b = (real && p.bias) ? p.bias[j] : 0.0f;
-        p.colp[j] = real ? make_float2(down, b) : make_float2(0.0f, -CUDART_INF_F);
-        p.ctab[(size_t)tile * 256 + r] = real ? down * kLog2e : 0.0f;
-        p.ctab[(size_t)tile * 256 + 128 + r] = real ? b * kLog2e : -CUDART_INF_F;
+        p.ctab[(size_t)tile * kCtabFloats + r] = real ? down : 0.0f;
+        p.ctab[(size_t)tile * kCtabFloats + kBlockN + r] = real ? b : -CUDART_INF_F;
     }
     uint8_t* img = p.btiles + (size_t)tile * (2 * kTileBytes);
 #pragma unroll
@@ -481,6 +527,374 @@ __global__ void __launch_bounds__(256) pack_f32_kernel(const PackParams p) {
     }
 }
 
+// Quantised weights: int8 tile number cc of this CTA, landed in slot cc % kI8Slots, is
+// expanded into fp16 stage cc % kStages8 (the MMA's B operand, 128-byte swizzle) by the 128
+// threads of warps 4-7. Each thread converts 8 chunks of 16 K slots: chunk i of warp w, lane l
+// is row 16 i + 8 (w / 2) + l % 8, K chunk 4 (w % 2) + l / 8 (see image8_offset). A byte
+// b = q + 128 becomes fp16 0x6400 | b = 1024 + b by a byte permute, minus 1152: exactly q.
+// False when a wait gave up (uniform per warp).
+__device__ __noinline__ bool expand_int8_tile(const HeadParams& p, uint32_t base, uint8_t* gbase, uint32_t cc, int w,
+                                              int lane) {
+    volatile uint32_t* abort_flag = reinterpret_cast<uint32_t*>(gbase + kOffMisc) + 1;
+    const uint32_t bars = base + kOffBars;
+    const uint32_t st = cc % (uint32_t)kStages8, i8 = cc % (uint32_t)kI8Slots;
+    bool ok = wait_bar(bars + 8u * (kBarI8Full + i8), (cc / kI8Slots) & 1u, abort_flag, p, 14);
+    ok = ok && wait_bar(bars + 8u * (kBarBEmpty + st), ((cc / kStages8) & 1u) ^ 1u, abort_flag, p, 15);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const int rlow = lane & 7, j0 = 2 * (lane >> 3);
+    const uint32_t src = base + kOffI8 + i8 * (uint32_t)kTile8Bytes + (uint32_t)(w * 32 + lane) * 16u;
+    const uint32_t dst = base + kOffB + st * (uint32_t)kTileBytes + (uint32_t)(w & 1) * 16384u +
+                         (uint32_t)(8 * (w >> 1) + rlow) * 128u;
+    const uint32_t o0 = (uint32_t)((j0 ^ rlow) << 4), o1 = (uint32_t)(((j0 + 1) ^ rlow) << 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint4 b = lds128u(src + 2048u * (uint32_t)i);
+        sts128u(dst + 2048u * (uint32_t)i + o0, make_uint4(q8_to_f16x2(b.x, 0x5140u), q8_to_f16x2(b.x, 0x7362u),
+                                                          q8_to_f16x2(b.y, 0x5140u), q8_to_f16x2(b.y, 0x7362u)));
+        sts128u(dst + 2048u * (uint32_t)i + o1, make_uint4(q8_to_f16x2(b.z, 0x5140u), q8_to_f16x2(b.z, 0x7362u),
+                                                          q8_to_f16x2(b.w, 0x5140u), q8_to_f16x2(b.w, 0x7362u)));
+    }
+    // every thread orders its stage writes before the tensor core's (async-proxy) reads, the
+    // warp synchronises, and one lane per warp releases the stage and the landing slot
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(bars + 8u * (kBarBFull + st));
+        mbar_arrive(bars + 8u * (kBarI8Empty + i8));
+    }
+    return true;
+}
+
+// ----------------------------------------------------- converter / expander warps (4-7)
+// A operand conversion per work unit and, for quantised weights, the int8 -> fp16 expansion of
+// every weight tile. Kept out of line: its registers are allocated apart from the epilogue's.
+__device__ __noinline__ void converter_warps(const HeadParams& p, uint32_t base, uint8_t* gbase, uint32_t tmem,
+                                             int warp, int lane) {
+    volatile uint32_t* abort_flag = reinterpret_cast<uint32_t*>(gbase + kOffMisc) + 1;
+    float* rho_s = reinterpret_cast<float*>(gbase + kOffRho);
+    uint32_t* qflag_s = reinterpret_cast<uint32_t*>(gbase + kOffQFlag);
+    auto bar = [&](int i) -> uint32_t { return base + kOffBars + 8u * (uint32_t)i; };
+    const int units = p.n_mblocks * p.n_splits;
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const int steps = p.hi_steps + p.lo_steps;
+    // Fast path (K % 4 == 0, 16-byte aligned features, and either the merged-tail layout of
+    // K = 113..120 or a layout without a merged tail): the 128 feature rows of the next unit
+    // are bulk-copied into shared memory while the current unit runs, so the A switch at a
+    // unit boundary is a shared-memory -> TMEM conversion.
+    const bool merged120 = p.hi_steps == 8 && p.lo_steps == 7 && p.merged_tail;
+    const bool kt = p.a_t > 0;  // [batch][k][T] input: gathered by the converters themselves
+    const bool staged = (merged120 || (!p.merged_tail && p.lo_steps == p.hi_steps)) && (p.k % 4) == 0 &&
+                        (kt || (reinterpret_cast<uintptr_t>(p.a) & 15u) == 0);
+    const bool bulk = staged && !kt;  // row-major: one bulk copy per unit
+    const uint32_t lo_col = 8u * (uint32_t)p.hi_steps;  // first TMEM column of the low part
+    const float* stage_g = reinterpret_cast<const float*>(gbase + kOffAStage);
+    auto issue_stage = [&](int u) {  // one thread: rows of unit u -> staging buffer
+        const Unit V = unit_of(u, p);
+        const long long r0 = (long long)V.mb * kBlockM;
+        const long long nrows = min((long long)kBlockM, p.m - r0);
+        const uint32_t bytes = (uint32_t)(nrows * p.k * 4);
+        mbar_arrive_expect_tx(bar(kBarStageFull), bytes);
+        bulk_copy_g2s(base + kOffAStage, p.a + r0 * p.k, bytes, bar(kBarStageFull));
+    };
+    // [batch][k][T]: thread r gathers row r of unit u into the staging buffer (for one k the
+    // 32 lanes of a warp read 32 consecutive timesteps: coalesced), while the previous unit runs.
+    float* my_stage = const_cast<float*>(stage_g) + (size_t)r * p.k;
+    auto gather_row = [&](int u) {
+        const Unit V = unit_of(u, p);
+        const long long row = (long long)V.mb * kBlockM + r;
+        if (row >= p.m) return;
+        const float* src = p.a + (row / p.a_t) * (long long)p.k * p.a_t + row % p.a_t;
+        for (int kk = 0; kk < p.k; ++kk) my_stage[kk] = __ldg(src + (long long)kk * p.a_t);
+    };
+    uint32_t staged_issued = 0, staged_used = 0;
+    if (bulk && r == 0 && (int)blockIdx.x < units) {
+        issue_stage(blockIdx.x);
+        staged_issued = 1;
+    }
+    if (staged && kt && (int)blockIdx.x < units) gather_row(blockIdx.x);
+    const long long astride = kt ? p.a_t : 1;
+    // A operand of unit u (the uc-th unit of this CTA) into TMEM; false when a wait gave up
+    // (the caller then leaves its loop as a whole warp).
+    auto convert_unit = [&](int u, uint32_t uc) -> bool {
+        const Unit U = unit_of(u, p);
+        const uint32_t slot = uc & 3u;
+        const long long row = (long long)U.mb * kBlockM + r;
+        const bool valid = row < p.m;
+        const long long vrow = valid ? row : 0;
+        const float* arow = staged ? stage_g + (size_t)r * p.k
+                            : kt ? p.a + (vrow / p.a_t) * (long long)p.k * p.a_t + vrow % p.a_t
+                                 : p.a + vrow * (long long)p.k;
+        if (bulk) {
+            if (!__all_sync(0xffffffffu, wait_bar(bar(kBarStageFull), uc & 1u, abort_flag, p, 12))) return false;
+            staged_used = uc + 1;
+        }
+        float max_abs = 0.0f;
+        if (valid) {
+            if (staged) {
+                for (int kk = 0; kk < p.k; kk += 4) {
+                    const float4 x = lds128(smem_u32(arow + kk));
+                    max_abs = fmaxf(max_abs, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+                }
+            } else {
+                for (int kk = 0; kk < p.k; ++kk) max_abs = fmaxf(max_abs, fabsf(__ldg(arow + (long long)kk * astride)));
+            }
+        }
+        // fp16 holds the parts only below 65504: rows with max|a| >= 2^14 are scaled by a
+        // power of two (exact) into [2^14, 2^15) and de-scaled in the epilogue.
+        float rs = 1.0f, rho = 1.0f;
+        if (max_abs >= 16384.0f && max_abs <= 3.4028235e38f) {
+            const int e = (int)((__float_as_uint(max_abs) >> 23) & 0xFFu) - 127;
+            rs = __uint_as_float((uint32_t)(127 + 14 - e) << 23);
+            rho = __uint_as_float((uint32_t)(127 + e - 14) << 23);
+        }
+        const uint32_t need = __ballot_sync(0xffffffffu, rs != 1.0f);
+        if (!__all_sync(0xffffffffu, wait_bar(bar(kBarAEmpty), (uc & 1u) ^ 1u, abort_flag, p, 5))) return false;
+        tc_fence_after();
+        const uint32_t a_t = tmem + lane_base + kTmemA;
+        if (staged) {
+            // pair p (K slots 2p, 2p+1): hi part -> column p; lo part -> column 8*hi_steps + p,
+            // except the merged tail of K = 113..120 (p = 56..59 -> columns 60..63).
+#pragma unroll 1
+            for (int j = 0; j < p.hi_steps; ++j) {
+                uint32_t hw[8], lw[8];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+                    const int kk = 16 * j + 8 * h;
+                    if (valid && kk < p.k) {
+                        x0 = lds128(smem_u32(arow + kk));
+                        if (kk + 4 < p.k) x1 = lds128(smem_u32(arow + kk + 4));
+                    }
+                    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        const float a0 = xs[2 * w] * rs, a1 = xs[2 * w + 1] * rs;
+                        const __half2 hv = __floats2half2_rn(a0, a1);
+                        const float2 hf = __half22float2(hv);
+                        const __half2 lv = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+                        hw[4 * h + w] = *reinterpret_cast<const uint32_t*>(&hv);
+                        lw[4 * h + w] = *reinterpret_cast<const uint32_t*>(&lv);
+                    }
+                }
+                if (!merged120 || j < 7) {
+                    tmem_st32x32b_x8(a_t + 8u * j, hw);
+                    tmem_st32x32b_x8(a_t + lo_col + 8u * j, lw);
+                } else {
+                    const uint32_t h4[4] = {hw[0], hw[1], hw[2], hw[3]};
+                    const uint32_t l4[4] = {lw[0], lw[1], lw[2], lw[3]};
+                    tmem_st32x32b_x4(a_t + 56u, h4);
+                    tmem_st32x32b_x4(a_t + 60u, l4);
+                }
+            }
+            if (bulk) mbar_arrive(bar(kBarStageRead));
+        } else {
+            for (int g4 = 0; g4 * 4 < steps; ++g4) {
+                uint32_t wv[32];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int step = g4 * 4 + t;
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) {
+                        uint32_t packed = 0u;
+                        if (step < steps) {
+                            const __half lo_h =
+                                a_part(arow, astride, valid, p.k, rs, step, 2 * w, p.hi_steps, p.merged_tail);
+                            const __half hi_h =
+                                a_part(arow, astride, valid, p.k, rs, step, 2 * w + 1, p.hi_steps, p.merged_tail);
+                            packed = (uint32_t)__half_as_ushort(lo_h) | ((uint32_t)__half_as_ushort(hi_h) << 16);
+                        }
+                        wv[t * 8 + w] = packed;
+                    }
+                }
+                tmem_st32x32b_x32(a_t + (uint32_t)g4 * 32u, wv);
+            }
+        }
+        tmem_st_wait();
+        rho_s[slot * 128 + r] = rho;
+        if (lane == 0) qflag_s[slot * 4 + q] = need;
+        tc_fence_before();
+        mbar_arrive(bar(kBarAFull));
+        mbar_arrive(bar(kBarRhoFull + (int)slot));
+        // next unit's rows into the staging buffer once every converter has read this one
+        if (staged && kt && u + (int)gridDim.x < units) gather_row(u + (int)gridDim.x);
+        bool stop = false;
+        if (bulk && r == 0 && u + (int)gridDim.x < units) {
+            if (wait_bar(bar(kBarStageRead), uc & 1u, abort_flag, p, 13)) {
+                issue_stage(u + (int)gridDim.x);
+                ++staged_issued;
+            } else {
+                stop = true;
+            }
+        }
+        return !__any_sync(0xffffffffu, stop);  // leave as a whole warp
+    };
+    auto expand_tile = [&](uint32_t cc) -> bool { return expand_int8_tile(p, base, gbase, cc, warp & 3, lane); };
+    if (!p.expand) {
+        uint32_t uc = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc)
+            if (!convert_unit(u, uc)) break;
+    } else {
+        // One ordered sequence of tile expansions with each unit's A conversion inserted
+        // right before the expansion of the unit's tile number kStages8 - 1: that expansion
+        // waits for a stage the unit's own MMAs free (which need the unit's A), while the
+        // conversion itself waits for the previous unit's MMAs (which need the expansions
+        // before it). So no wait can depend on a later step of this sequence.
+        int au = blockIdx.x;       // next unit whose A is converted
+        uint32_t auc = 0, a_first = 0;  // its number within this CTA, its first tile number
+        uint32_t cc = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+            const Unit U = unit_of(u, p);
+            for (int c = U.c0; ok && c < U.c1; ++c, ++cc) {
+                if (au < units && cc == a_first + (uint32_t)kStages8 - 1u) {
+                    const Unit A = unit_of(au, p);
+                    ok = convert_unit(au, auc);
+                    a_first += (uint32_t)(A.c1 - A.c0);
+                    au += gridDim.x;
+                    ++auc;
+                }
+                ok = ok && expand_tile(cc);
+            }
+        }
+        for (; ok && au < units; au += gridDim.x, ++auc) ok = convert_unit(au, auc);
+    }
+    // a staged copy still in flight must land before the CTA exits
+    if (bulk && r == 0 && staged_issued > staged_used) drain_bar(bar(kBarStageFull), (staged_issued - 1) & 1u, p);
+}
+
+// ------------------------------------------------------------ epilogue warps (8-31)
+template <bool EMIT_LOGITS, int NPOLY>
+__device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, uint8_t* gbase, uint32_t tmem,
+                                            int warp, int lane) {
+    volatile uint32_t* abort_flag = reinterpret_cast<uint32_t*>(gbase + kOffMisc) + 1;
+    float* rho_s = reinterpret_cast<float*>(gbase + kOffRho);
+    uint32_t* qflag_s = reinterpret_cast<uint32_t*>(gbase + kOffQFlag);
+    float4* merge_s = reinterpret_cast<float4*>(gbase + kOffMerge);
+    auto bar = [&](int i) -> uint32_t { return base + kOffBars + 8u * (uint32_t)i; };
+    const int units = p.n_mblocks * p.n_splits;
+    // ------------------------------------------------------------- epilogue
+    // Each quarter is one 32-column TMEM load; the accumulator goes back to the MMA
+    // issuer once its four quarters are loaded, and the math runs from registers. Six
+    // groups give every SM sub-partition six independent warps of softmax work; a group
+    // sees a different column subset of each row, which the online update and the merge
+    // at the end of the unit do not mind.
+    const int g = (warp - 8) >> 2;
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint32_t cc0 = 0, uc = 0;  // tiles before this unit, units so far
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
+        const Unit U = unit_of(u, p);
+        const uint32_t ntile = (uint32_t)(U.c1 - U.c0);
+        const uint32_t slot = uc & 3u;
+        const long long row = (long long)U.mb * kBlockM + r;
+        RowState st{-CUDART_INF_F, 0.0f, -CUDART_INF_F, 0, -CUDART_INF_F};
+        const uint32_t tag = uc + 1u;  // row thresholds of earlier units carry smaller tags
+        const uint32_t rowmax = base + kOffRowMax + 8u * (uint32_t)r;
+        if (!__all_sync(0xffffffffu, wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6))) break;
+        const float rho = rho_s[slot * 128 + r];
+        const bool scaled = qflag_s[slot * 4 + q] != 0u;
+        // this group's quarters of the unit: Q = 4*(tile within the unit) + k, Q % 6 == g
+        // (numbered from each unit's start, so a row's summation order depends only on
+        // its unit's tile range, not on which CTA runs the unit or what it ran before).
+        const uint32_t qe = 4u * ntile;
+        bool first = true;
+        for (uint32_t Q = (uint32_t)g; Q < qe; Q += kEpiGroups) {
+            const uint32_t k = Q & 3u;
+            // ring positions of this tile: accumulator buffer and class-table slot, with phases
+            const uint32_t cc = cc0 + (Q >> 2);
+            const uint32_t buf = cc % kAccBufs, aph = (cc / kAccBufs) & 1u;
+            const uint32_t cslot = cc % kCtabSlots, cph = (cc / kCtabSlots) & 1u;
+            const int c = U.c0 + (int)(Q >> 2);
+            if (!EMIT_LOGITS &&
+                !__all_sync(0xffffffffu, wait_bar(bar(kBarCtabFull + (int)cslot), cph, abort_flag, p, 11))) {
+                ok = false;
+                break;
+            }
+            if (!__all_sync(0xffffffffu, wait_bar(bar(kBarAccFull + (int)buf), aph, abort_flag, p, 7))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t v[32];
+            tmem_ld32x32b_x32_wait(tmem + lane_base + kTmemAcc + buf * 128u + 32u * k, v);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarAccEmpty + (int)buf));
+            const int col0 = c * kBlockN + 32 * (int)k;
+            if (EMIT_LOGITS) {
+                const float* cp = p.ctab + (size_t)c * 256 + 32 * k;
+                float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
+                if (row < p.m) {
+                    if (scaled) logits_quarter<true>(v, cp, col0, rho, out_row, p.n);
+                    else logits_quarter<false>(v, cp, col0, rho, out_row, p.n);
+                }
+            } else {
+                const uint32_t cs = base + kOffCtab + cslot * kCtabBytes + 4u * 32u * k;
+                if (first) {
+                    if (scaled)
+                        fused_quarter<true, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                    else
+                        fused_quarter<false, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                } else {
+                    if (scaled)
+                        fused_quarter<true, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                    else
+                        fused_quarter<false, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                }
+                first = false;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarCtabEmpty + (int)cslot));
+            }
+        }
+        if (!ok) break;
+        cc0 += ntile;
+        if (!EMIT_LOGITS) {
+            // Merge the groups' partial rows for this unit through shared memory.
+            const uint32_t mb2 = uc & 1u;
+            float4* mg = merge_s + mb2 * (kEpiGroups - 1) * 128;
+            if (g != 0) {
+                if (!__all_sync(0xffffffffu, wait_bar(bar(kBarMEmpty + (int)mb2), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 8)))
+                    break;
+                mg[(g - 1) * 128 + r] = make_float4(st.off, st.sum, st.best, __int_as_float(st.idx));
+                mbar_arrive(bar(kBarMFull + (int)mb2));
+            } else {
+                if (!__all_sync(0xffffffffu, wait_bar(bar(kBarMFull + (int)mb2), (uc >> 1) & 1u, abort_flag, p, 9))) break;
+                float4 o[kEpiGroups - 1];
+#pragma unroll
+                for (int j = 0; j < kEpiGroups - 1; ++j) o[j] = mg[j * 128 + r];
+                mbar_arrive(bar(kBarMEmpty + (int)mb2));
+                // Unit maximum = the largest tracked best (the group holding the maximum
+                // always tracks it); the argmax comes from the group(s) whose best equals
+                // it (ties: lower class index); each sum is rescaled from its own offset.
+                float M = st.best;
+#pragma unroll
+                for (int j = 0; j < kEpiGroups - 1; ++j) M = fmaxf(M, o[j].z);
+                float S = st.off != -CUDART_INF_F ? st.sum * ex2_approx(st.off - M) : 0.0f;
+                int I = st.best == M ? st.idx : 0x7fffffff;
+#pragma unroll
+                for (int j = 0; j < kEpiGroups - 1; ++j) {
+                    if (o[j].x != -CUDART_INF_F) S += o[j].y * ex2_approx(o[j].x - M);
+                    if (o[j].z == M) I = min(I, __float_as_int(o[j].w));
+                }
+                if (I == 0x7fffffff) I = 0;  // no class at all (cannot happen for a real unit)
+                if (row < p.m) {
+                    if (p.n_splits == 1) {
+                        p.idx[row] = I;
+                        p.prob[row] = 1.0f / S;
+                    } else {
+                        p.partial[(size_t)U.sp * (size_t)p.m + (size_t)row] =
+                            make_float4(M, S, __int_as_float(I), 0.0f);
+                    }
+                }
+            }
+        }
+    }
+}
+
 // -------------------------------------------------------------------- head
 // Warp roles (one CTA per SM, persistent over work units = (row block, class range)):
 //   warp 0      lane 0: weight-tile producer (TMA bulk copies into the smem ring)
@@ -499,9 +913,6 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
     uint8_t* gbase = smem_raw + (base - raw_u32);
     uint32_t* misc = reinterpret_cast<uint32_t*>(gbase + kOffMisc);
     volatile uint32_t* abort_flag = misc + 1;
-    float* rho_s = reinterpret_cast<float*>(gbase + kOffRho);
-    uint32_t* qflag_s = reinterpret_cast<uint32_t*>(gbase + kOffQFlag);
-    float4* merge_s = reinterpret_cast<float4*>(gbase + kOffMerge);
     auto bar = [&](int i) -> uint32_t { return base + kOffBars + 8u * (uint32_t)i; };
 
     const int warp = threadIdx.x >> 5;
@@ -509,9 +920,14 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
     const int units = p.n_mblocks * p.n_splits;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(bar(kBarBFull + s), 1);
+        for (int s = 0; s < kMaxStages; ++s) {
+            // int8 tiles: the expander warps fill a stage; otherwise one bulk copy (transaction bytes)
+            mbar_init(bar(kBarBFull + s), p.expand ? kExpanderWarps : 1);
             mbar_init(bar(kBarBEmpty + s), 1);
+        }
+        for (int s = 0; s < kI8Slots; ++s) {
+            mbar_init(bar(kBarI8Full + s), 1);
+            mbar_init(bar(kBarI8Empty + s), kExpanderWarps);
         }
         mbar_init(bar(kBarAFull), 128);
         mbar_init(bar(kBarAEmpty), 1);
@@ -519,7 +935,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         mbar_init(bar(kBarStageRead), 128);
         for (int i = 0; i < kAccBufs; ++i) {
             mbar_init(bar(kBarAccFull + i), 1);
-            mbar_init(bar(kBarAccEmpty + i), 512);
+            mbar_init(bar(kBarAccEmpty + i), 16);  // one arrival per epilogue warp and quarter
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(kBarMFull + i), 128 * (kEpiGroups - 1));
@@ -527,8 +943,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         }
         for (int i = 0; i < 4; ++i) {
             mbar_init(bar(kBarRhoFull + i), 128);
-            mbar_init(bar(kBarCtabFull + i), 1);
-            mbar_init(bar(kBarCtabEmpty + i), 512);
+            mbar_init(bar(kBarCtabFull + i), 1);    // one lane of the class-table warp
+            mbar_init(bar(kBarCtabEmpty + i), 16);  // one arrival per epilogue warp and quarter
+            mbar_init(bar(kBarCtabRaw + i), 1);
         }
         mbar_init(bar(kBarMmaDone), 1);
         misc[1] = 0u;
@@ -549,32 +966,37 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         // The whole warp runs the loop (uniform control flow); one elected lane issues.
-        // FP32 weights: each tile is a 64 KB (hi, lo) pair, so the ring has half as many stages.
-        const uint32_t tile_bytes = p.dual ? 2u * kTileBytes : kTileBytes;
-        const uint32_t nst = p.dual ? kStages / 2 : kStages;
+        // fp16 image and FP32 weights: each tile (32 KB, or 64 KB for the FP32 (hi, lo) pair)
+        // goes straight into an fp16 stage. int8 tiles: each 16 KB tile goes into a landing slot,
+        // which the expander warps turn into an fp16 stage.
+        const uint32_t ring = p.expand ? (uint32_t)kI8Slots : p.dual ? (uint32_t)kStagesDual : (uint32_t)kStagesImage;
+        const uint32_t tile_bytes = p.expand ? (uint32_t)kTile8Bytes : p.dual ? 2u * kTileBytes : (uint32_t)kTileBytes;
+        const uint32_t dst0 = base + (p.expand ? kOffI8 : kOffB);
+        const int bar_full = p.expand ? kBarI8Full : kBarBFull;
+        const int bar_empty = p.expand ? kBarI8Empty : kBarBEmpty;
         uint32_t cc = 0, issued = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
             const Unit U = unit_of(u, p);
             for (int c = U.c0; c < U.c1; ++c, ++cc) {
-                const int s = (int)(cc % nst);
+                const int s = (int)(cc % ring);
                 ok = __all_sync(0xffffffffu,
-                                wait_bar(bar(kBarBEmpty + s), ((cc / nst) & 1u) ^ 1u, abort_flag, p, 1));
+                                wait_bar(bar(bar_empty + s), ((cc / ring) & 1u) ^ 1u, abort_flag, p, 1));
                 if (!ok) break;
                 if (p.debug_flags & kDebugStallProducer) continue;
                 if (elect_one()) {
-                    mbar_arrive_expect_tx(bar(kBarBFull + s), tile_bytes);
-                    bulk_copy_g2s(base + kOffB + (uint32_t)s * tile_bytes, p.btiles + (size_t)c * tile_bytes, tile_bytes,
-                                  bar(kBarBFull + s));
+                    mbar_arrive_expect_tx(bar(bar_full + s), tile_bytes);
+                    bulk_copy_g2s(dst0 + (uint32_t)s * tile_bytes, p.btiles + (size_t)c * tile_bytes, tile_bytes,
+                                  bar(bar_full + s));
                 }
                 __syncwarp();
                 issued = cc + 1;
             }
         }
-        // Drain: the last copy issued into each stage must land before the CTA exits.
-        for (uint32_t s = 0; s < nst && s < issued; ++s) {
-            const uint32_t fills = (issued - 1 - s) / nst + 1;
-            drain_bar(bar(kBarBFull + (int)s), (fills - 1) & 1u, p);
+        // Drain: the last copy issued into each slot must land before the CTA exits.
+        for (uint32_t s = 0; s < ring && s < issued; ++s) {
+            const uint32_t fills = (issued - 1 - s) / ring + 1;
+            drain_bar(bar(bar_full + (int)s), (fills - 1) & 1u, p);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA issuer
@@ -590,8 +1012,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             const int kc = step < p.hi_steps ? step : step - p.hi_steps;
             boff[step] = ((uint32_t)(kc >> 2) * 16384u + (uint32_t)(kc & 3) * 32u) >> 4;
         }
-        const uint32_t tile_bytes = p.dual ? 2u * kTileBytes : kTileBytes;
-        const uint32_t nst = p.dual ? kStages / 2 : kStages;
+        const uint32_t tile_bytes = p.dual ? 2u * kTileBytes : kTileBytes;  // one fp16 stage
+        const uint32_t nst = p.dual ? (uint32_t)kStagesDual : p.expand ? (uint32_t)kStages8 : (uint32_t)kStagesImage;
         uint32_t cc = 0, uc = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
@@ -653,305 +1075,51 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         drain_bar(bar(kBarMmaDone), 0u, p);
     } else if (warp == 2) {
         // ---------------------------------------------------- class-table producer
+        // Per tile: the weight's (scale[128], bias[128]) land in a ring slot by one bulk copy,
+        // then the warp converts them in place to log2 units, c = scale * log2(e) and
+        // e = bias * log2(e), which the epilogue's t = D * c + e needs.
         if (!EMIT_LOGITS) {
-            uint32_t cc = 0, issued = 0;
+            uint32_t cc = 0, pending = 0;  // pending: 1 + slot of a copy not yet seen landing
             bool ok = true;
             for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
                 const Unit U = unit_of(u, p);
                 for (int c = U.c0; c < U.c1; ++c, ++cc) {
                     const uint32_t slot = cc % kCtabSlots;
-                    ok = __all_sync(0xffffffffu, wait_bar(bar(kBarCtabEmpty + (int)slot),
-                                                          ((cc / kCtabSlots) & 1u) ^ 1u, abort_flag, p, 10));
+                    const uint32_t ph = (cc / kCtabSlots) & 1u;
+                    ok = __all_sync(0xffffffffu, wait_bar(bar(kBarCtabEmpty + (int)slot), ph ^ 1u, abort_flag, p, 10));
                     if (!ok) break;
+                    const uint32_t dst = base + kOffCtab + slot * kCtabBytes;
                     if (elect_one()) {
-                        mbar_arrive_expect_tx(bar(kBarCtabFull + (int)slot), kCtabBytes);
-                        bulk_copy_g2s(base + kOffCtab + slot * kCtabBytes, p.ctab + (size_t)c * 256, kCtabBytes,
-                                      bar(kBarCtabFull + (int)slot));
+                        mbar_arrive_expect_tx(bar(kBarCtabRaw + (int)slot), kCtabBytes);
+                        bulk_copy_g2s(dst, p.ctab + (size_t)c * kCtabFloats, kCtabBytes, bar(kBarCtabRaw + (int)slot));
                     }
                     __syncwarp();
-                    issued = cc + 1;
+                    pending = slot + 1u;
+                    ok = __all_sync(0xffffffffu, wait_bar(bar(kBarCtabRaw + (int)slot), ph, abort_flag, p, 16));
+                    if (!ok) break;
+                    pending = 0u;
+                    float4 sc = lds128(dst + 16u * lane);
+                    float4 bi = lds128(dst + 512u + 16u * lane);
+                    sc = make_float4(sc.x * kLog2e, sc.y * kLog2e, sc.z * kLog2e, sc.w * kLog2e);
+                    bi = make_float4(bi.x * kLog2e, bi.y * kLog2e, bi.z * kLog2e, bi.w * kLog2e);
+                    sts128(dst + 16u * lane, sc);
+                    sts128(dst + 512u + 16u * lane, bi);
+                    // the slot is next overwritten by a bulk copy (async proxy); every lane's
+                    // writes are ordered before the one arrival by the warp synchronisation
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(kBarCtabFull + (int)slot));
                 }
             }
-            for (uint32_t s = 0; s < kCtabSlots && s < issued; ++s) {
-                const uint32_t fills = (issued - 1 - s) / kCtabSlots + 1;
-                drain_bar(bar(kBarCtabFull + (int)s), (fills - 1) & 1u, p);
+            if (pending) {  // a copy in flight when another role aborted must land before exit
+                const uint32_t slot = pending - 1u;
+                drain_bar(bar(kBarCtabRaw + (int)slot), ((cc / kCtabSlots) & 1u), p);
             }
         }
     } else if (warp >= 4 && warp < 8) {
-        // ----------------------------------------------------------- converters
-        const int q = warp & 3;
-        const int r = q * 32 + lane;
-        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        const int steps = p.hi_steps + p.lo_steps;
-        // Fast path (K % 4 == 0, 16-byte aligned features, and either the merged-tail layout of
-        // K = 113..120 or a layout without a merged tail): the 128 feature rows of the next unit
-        // are bulk-copied into shared memory while the current unit runs, so the A switch at a
-        // unit boundary is a shared-memory -> TMEM conversion.
-        const bool merged120 = p.hi_steps == 8 && p.lo_steps == 7 && p.merged_tail;
-        const bool kt = p.a_t > 0;  // [batch][k][T] input: gathered by the converters themselves
-        const bool staged = (merged120 || (!p.merged_tail && p.lo_steps == p.hi_steps)) && (p.k % 4) == 0 &&
-                            (kt || (reinterpret_cast<uintptr_t>(p.a) & 15u) == 0);
-        const bool bulk = staged && !kt;  // row-major: one bulk copy per unit
-        const uint32_t lo_col = 8u * (uint32_t)p.hi_steps;  // first TMEM column of the low part
-        const float* stage_g = reinterpret_cast<const float*>(gbase + kOffAStage);
-        auto issue_stage = [&](int u) {  // one thread: rows of unit u -> staging buffer
-            const Unit V = unit_of(u, p);
-            const long long r0 = (long long)V.mb * kBlockM;
-            const long long nrows = min((long long)kBlockM, p.m - r0);
-            const uint32_t bytes = (uint32_t)(nrows * p.k * 4);
-            mbar_arrive_expect_tx(bar(kBarStageFull), bytes);
-            bulk_copy_g2s(base + kOffAStage, p.a + r0 * p.k, bytes, bar(kBarStageFull));
-        };
-        // [batch][k][T]: thread r gathers row r of unit u into the staging buffer (for one k the
-        // 32 lanes of a warp read 32 consecutive timesteps: coalesced), while the previous unit runs.
-        float* my_stage = const_cast<float*>(stage_g) + (size_t)r * p.k;
-        auto gather_row = [&](int u) {
-            const Unit V = unit_of(u, p);
-            const long long row = (long long)V.mb * kBlockM + r;
-            if (row >= p.m) return;
-            const float* src = p.a + (row / p.a_t) * (long long)p.k * p.a_t + row % p.a_t;
-            for (int kk = 0; kk < p.k; ++kk) my_stage[kk] = __ldg(src + (long long)kk * p.a_t);
-        };
-        uint32_t staged_issued = 0, staged_used = 0;
-        if (bulk && r == 0 && (int)blockIdx.x < units) {
-            issue_stage(blockIdx.x);
-            staged_issued = 1;
-        }
-        if (staged && kt && (int)blockIdx.x < units) gather_row(blockIdx.x);
-        const long long astride = kt ? p.a_t : 1;
-        uint32_t uc = 0;
-        for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc) {
-            const Unit U = unit_of(u, p);
-            const uint32_t slot = uc & 3u;
-            const long long row = (long long)U.mb * kBlockM + r;
-            const bool valid = row < p.m;
-            const long long vrow = valid ? row : 0;
-            const float* arow = staged ? stage_g + (size_t)r * p.k
-                                : kt ? p.a + (vrow / p.a_t) * (long long)p.k * p.a_t + vrow % p.a_t
-                                     : p.a + vrow * (long long)p.k;
-            if (bulk) {
-                if (!__all_sync(0xffffffffu, wait_bar(bar(kBarStageFull), uc & 1u, abort_flag, p, 12))) break;
-                staged_used = uc + 1;
-            }
-            float max_abs = 0.0f;
-            if (valid) {
-                if (staged) {
-                    for (int kk = 0; kk < p.k; kk += 4) {
-                        const float4 x = lds128(smem_u32(arow + kk));
-                        max_abs = fmaxf(max_abs, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-                    }
-                } else {
-                    for (int kk = 0; kk < p.k; ++kk) max_abs = fmaxf(max_abs, fabsf(__ldg(arow + (long long)kk * astride)));
-                }
-            }
-            // fp16 holds the parts only below 65504: rows with max|a| >= 2^14 are scaled by a
-            // power of two (exact) into [2^14, 2^15) and de-scaled in the epilogue.
-            float rs = 1.0f, rho = 1.0f;
-            if (max_abs >= 16384.0f && max_abs <= 3.4028235e38f) {
-                const int e = (int)((__float_as_uint(max_abs) >> 23) & 0xFFu) - 127;
-                rs = __uint_as_float((uint32_t)(127 + 14 - e) << 23);
-                rho = __uint_as_float((uint32_t)(127 + e - 14) << 23);
-            }
-            const uint32_t need = __ballot_sync(0xffffffffu, rs != 1.0f);
-            if (!__all_sync(0xffffffffu, wait_bar(bar(kBarAEmpty), (uc & 1u) ^ 1u, abort_flag, p, 5))) break;
-            tc_fence_after();
-            const uint32_t a_t = tmem + lane_base + kTmemA;
-            if (staged) {
-                // pair p (K slots 2p, 2p+1): hi part -> column p; lo part -> column 8*hi_steps + p,
-                // except the merged tail of K = 113..120 (p = 56..59 -> columns 60..63).
-#pragma unroll 1
-                for (int j = 0; j < p.hi_steps; ++j) {
-                    uint32_t hw[8], lw[8];
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-                        const int kk = 16 * j + 8 * h;
-                        if (valid && kk < p.k) {
-                            x0 = lds128(smem_u32(arow + kk));
-                            if (kk + 4 < p.k) x1 = lds128(smem_u32(arow + kk + 4));
-                        }
-                        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            const float a0 = xs[2 * w] * rs, a1 = xs[2 * w + 1] * rs;
-                            const __half2 hv = __floats2half2_rn(a0, a1);
-                            const float2 hf = __half22float2(hv);
-                            const __half2 lv = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
-                            hw[4 * h + w] = *reinterpret_cast<const uint32_t*>(&hv);
-                            lw[4 * h + w] = *reinterpret_cast<const uint32_t*>(&lv);
-                        }
-                    }
-                    if (!merged120 || j < 7) {
-                        tmem_st32x32b_x8(a_t + 8u * j, hw);
-                        tmem_st32x32b_x8(a_t + lo_col + 8u * j, lw);
-                    } else {
-                        const uint32_t h4[4] = {hw[0], hw[1], hw[2], hw[3]};
-                        const uint32_t l4[4] = {lw[0], lw[1], lw[2], lw[3]};
-                        tmem_st32x32b_x4(a_t + 56u, h4);
-                        tmem_st32x32b_x4(a_t + 60u, l4);
-                    }
-                }
-                if (bulk) mbar_arrive(bar(kBarStageRead));
-            } else {
-                for (int g4 = 0; g4 * 4 < steps; ++g4) {
-                    uint32_t wv[32];
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const int step = g4 * 4 + t;
-#pragma unroll
-                        for (int w = 0; w < 8; ++w) {
-                            uint32_t packed = 0u;
-                            if (step < steps) {
-                                const __half lo_h =
-                                    a_part(arow, astride, valid, p.k, rs, step, 2 * w, p.hi_steps, p.merged_tail);
-                                const __half hi_h =
-                                    a_part(arow, astride, valid, p.k, rs, step, 2 * w + 1, p.hi_steps, p.merged_tail);
-                                packed = (uint32_t)__half_as_ushort(lo_h) | ((uint32_t)__half_as_ushort(hi_h) << 16);
-                            }
-                            wv[t * 8 + w] = packed;
-                        }
-                    }
-                    tmem_st32x32b_x32(a_t + (uint32_t)g4 * 32u, wv);
-                }
-            }
-            tmem_st_wait();
-            rho_s[slot * 128 + r] = rho;
-            if (lane == 0) qflag_s[slot * 4 + q] = need;
-            tc_fence_before();
-            mbar_arrive(bar(kBarAFull));
-            mbar_arrive(bar(kBarRhoFull + (int)slot));
-            // next unit's rows into the staging buffer once every converter has read this one
-            if (staged && kt && u + (int)gridDim.x < units) gather_row(u + (int)gridDim.x);
-            bool stop = false;
-            if (bulk && r == 0 && u + (int)gridDim.x < units) {
-                if (wait_bar(bar(kBarStageRead), uc & 1u, abort_flag, p, 13)) {
-                    issue_stage(u + (int)gridDim.x);
-                    ++staged_issued;
-                } else {
-                    stop = true;
-                }
-            }
-            if (__any_sync(0xffffffffu, stop)) break;  // leave the loop as a whole warp
-        }
-        // a staged copy still in flight must land before the CTA exits
-        if (bulk && r == 0 && staged_issued > staged_used) drain_bar(bar(kBarStageFull), (staged_issued - 1) & 1u, p);
+        converter_warps(p, base, gbase, tmem, warp, lane);
     } else if (warp >= 8) {
-        // ------------------------------------------------------------- epilogue
-        // Each quarter is one 32-column TMEM load; the accumulator goes back to the MMA
-        // issuer once its four quarters are loaded, and the math runs from registers. Six
-        // groups give every SM sub-partition six independent warps of softmax work; a group
-        // sees a different column subset of each row, which the online update and the merge
-        // at the end of the unit do not mind.
-        const int g = (warp - 8) >> 2;
-        const int q = warp & 3;
-        const int r = q * 32 + lane;
-        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        uint32_t cc0 = 0, uc = 0;  // tiles before this unit, units so far
-        bool ok = true;
-        for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
-            const Unit U = unit_of(u, p);
-            const uint32_t ntile = (uint32_t)(U.c1 - U.c0);
-            const uint32_t slot = uc & 3u;
-            const long long row = (long long)U.mb * kBlockM + r;
-            RowState st{-CUDART_INF_F, 0.0f, -CUDART_INF_F, 0, -CUDART_INF_F};
-            const uint32_t tag = uc + 1u;  // row thresholds of earlier units carry smaller tags
-            const uint32_t rowmax = base + kOffRowMax + 8u * (uint32_t)r;
-            if (!__all_sync(0xffffffffu, wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6))) break;
-            const float rho = rho_s[slot * 128 + r];
-            const bool scaled = qflag_s[slot * 4 + q] != 0u;
-            // this group's quarters of the unit: Q = 4*(tile within the unit) + k, Q % 6 == g
-            // (numbered from each unit's start, so a row's summation order depends only on
-            // its unit's tile range, not on which CTA runs the unit or what it ran before)
-            const uint32_t qe = 4u * ntile;
-            bool first = true;
-            for (uint32_t Q = (uint32_t)g; Q < qe; Q += kEpiGroups) {
-                const uint32_t cc = cc0 + (Q >> 2), k = Q & 3u;
-                const int c = U.c0 + (int)(Q >> 2);
-                const uint32_t buf = cc % kAccBufs;
-                const uint32_t cslot = cc % kCtabSlots;
-                if (!EMIT_LOGITS &&
-                    !__all_sync(0xffffffffu,
-                                wait_bar(bar(kBarCtabFull + (int)cslot), (cc / kCtabSlots) & 1u, abort_flag, p, 11))) {
-                    ok = false;
-                    break;
-                }
-                if (!__all_sync(0xffffffffu, wait_bar(bar(kBarAccFull + (int)buf), (cc / kAccBufs) & 1u, abort_flag, p, 7))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                uint32_t v[32];
-                tmem_ld32x32b_x32_wait(tmem + lane_base + kTmemAcc + buf * 128u + 32u * k, v);
-                tc_fence_before();
-                mbar_arrive(bar(kBarAccEmpty + (int)buf));
-                const int col0 = c * kBlockN + 32 * (int)k;
-                if (EMIT_LOGITS) {
-                    const float2* cp = p.colp + (size_t)col0;
-                    float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
-                    if (row < p.m) {
-                        if (scaled) logits_quarter<true>(v, cp, col0, rho, out_row, p.n);
-                        else logits_quarter<false>(v, cp, col0, rho, out_row, p.n);
-                    }
-                } else {
-                    const uint32_t cs = base + kOffCtab + cslot * kCtabBytes + 4u * 32u * k;
-                    if (first) {
-                        if (scaled)
-                            fused_quarter<true, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
-                        else
-                            fused_quarter<false, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
-                    } else {
-                        if (scaled)
-                            fused_quarter<true, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
-                        else
-                            fused_quarter<false, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
-                    }
-                    first = false;
-                    mbar_arrive(bar(kBarCtabEmpty + (int)cslot));
-                }
-            }
-            if (!ok) break;
-            cc0 += ntile;
-            if (!EMIT_LOGITS) {
-                // Merge the groups' partial rows for this unit through shared memory.
-                const uint32_t mb2 = uc & 1u;
-                float4* mg = merge_s + mb2 * (kEpiGroups - 1) * 128;
-                if (g != 0) {
-                    if (!__all_sync(0xffffffffu, wait_bar(bar(kBarMEmpty + (int)mb2), ((uc >> 1) & 1u) ^ 1u, abort_flag, p, 8)))
-                        break;
-                    mg[(g - 1) * 128 + r] = make_float4(st.off, st.sum, st.best, __int_as_float(st.idx));
-                    mbar_arrive(bar(kBarMFull + (int)mb2));
-                } else {
-                    if (!__all_sync(0xffffffffu, wait_bar(bar(kBarMFull + (int)mb2), (uc >> 1) & 1u, abort_flag, p, 9))) break;
-                    float4 o[kEpiGroups - 1];
-#pragma unroll
-                    for (int j = 0; j < kEpiGroups - 1; ++j) o[j] = mg[j * 128 + r];
-                    mbar_arrive(bar(kBarMEmpty + (int)mb2));
-                    // Unit maximum = the largest tracked best (the group holding the maximum
-                    // always tracks it); the argmax comes from the group(s) whose best equals
-                    // it (ties: lower class index); each sum is rescaled from its own offset.
-                    float M = st.best;
-#pragma unroll
-                    for (int j = 0; j < kEpiGroups - 1; ++j) M = fmaxf(M, o[j].z);
-                    float S = st.off != -CUDART_INF_F ? st.sum * ex2_approx(st.off - M) : 0.0f;
-                    int I = st.best == M ? st.idx : 0x7fffffff;
-#pragma unroll
-                    for (int j = 0; j < kEpiGroups - 1; ++j) {
-                        if (o[j].x != -CUDART_INF_F) S += o[j].y * ex2_approx(o[j].x - M);
-                        if (o[j].z == M) I = min(I, __float_as_int(o[j].w));
-                    }
-                    if (I == 0x7fffffff) I = 0;  // no class at all (cannot happen for a real unit)
-                    if (row < p.m) {
-                        if (p.n_splits == 1) {
-                            p.idx[row] = I;
-                            p.prob[row] = 1.0f / S;
-                        } else {
-                            p.partial[(size_t)U.sp * (size_t)p.m + (size_t)row] =
-                                make_float4(M, S, __int_as_float(I), 0.0f);
-                        }
-                    }
-                }
-            }
-        }
+        epilogue_warps<EMIT_LOGITS, NPOLY>(p, base, gbase, tmem, warp, lane);
     }
 
     tc_fence_before();

@@ -102,9 +102,14 @@ class QuantizedWeight:
         self._bias = None if bias is None else _f32(bias).copy()
 
     @classmethod
-    def from_f32_transposed(cls, w_t, ctx: Context | None = None, bias=None) -> "QuantizedWeight":
+    def from_f32_transposed(cls, w_t, ctx: Context | None = None, bias=None,
+                            compact: bool = False) -> "QuantizedWeight":
         """Pack the transposed weight w_t [N, K] (QuantizedWeight::from_f32_transposed), with
-        an optional bias folded in (the Add.204 fold, src/engine/model.rs:141-155)."""
+        an optional bias folded in (the Add.204 fold, src/engine/model.rs:141-155).
+
+        compact=False keeps the fp16 image of the tensor-core operand in HBM (rh_weight_pack,
+        the faster head); compact=True keeps int8 tiles, expanded in shared memory
+        (rh_weight_pack_compact: the reference's >= 3.5x footprint cut, same results)."""
         ctx = ctx or default_context()
         w_t = _f32(w_t)
         if w_t.ndim != 2:
@@ -112,8 +117,9 @@ class QuantizedWeight:
         n, k = w_t.shape
         b = None if bias is None else _f32(bias).reshape(-1)
         h = ctypes.c_void_p()
-        check(load().rh_weight_pack(ctx.handle, _p(w_t), n, k, None if b is None else _p(b),
-                                    0 if b is None else b.size, ctypes.byref(h)))
+        fn = load().rh_weight_pack_compact if compact else load().rh_weight_pack
+        check(fn(ctx.handle, _p(w_t), n, k, None if b is None else _p(b), 0 if b is None else b.size,
+                 ctypes.byref(h)))
         return cls(ctx, h, n, k, b)
 
     @classmethod
@@ -140,13 +146,15 @@ class QuantizedWeight:
         check(load().rh_weight_export(self._ctx.handle, self.handle, None, _p(s)))
         return s
 
-    def tensor_core_image(self):
-        """(tiles uint8 [n_chunks, 32768], colp f32 [n_chunks*128, 2]) as laid out on the device."""
+    def device_image(self):
+        """(tiles uint8 [n_chunks, tile bytes], table f32 [n_chunks, 2, 128]) as held on the
+        device: the tiles (fp16 operand image, or compact int8 q + 128 in the kernel's expansion
+        order; layouts in include/rechead.h) and, per tile, the classes' scales then biases."""
         n_chunks = (self.rows + 127) // 128
-        tiles = np.empty((n_chunks, 32768), np.uint8)
-        colp = np.empty((n_chunks * 128, 2), np.float32)
-        check(load().rh_weight_export_image(self._ctx.handle, self.handle, _p(tiles), _p(colp)))
-        return tiles, colp
+        tiles = np.empty((n_chunks, int(load().rh_weight_tile_bytes(self.handle))), np.uint8)
+        table = np.empty((n_chunks, 2, 128), np.float32)
+        check(load().rh_weight_export_image(self._ctx.handle, self.handle, _p(tiles), _p(table)))
+        return tiles, table
 
     @property
     def device_bytes(self) -> int:

@@ -91,46 +91,116 @@ def test_pack_bit_exact_vs_oracle(rh, ctx, oracle, n, k):
     assert np.array_equal(qw.scales.view(np.uint32), s.view(np.uint32))
 
 
-def expected_image(q: np.ndarray, scales: np.ndarray, bias, k: int):
-    """The tensor-core image restated on the host: per 128-class tile, two 16 KB K-blocks of
-    128 rows x 128 bytes, 16-byte chunks XOR-swizzled by row % 8; K slots >= k are zero and,
-    when the last 16-wide K step holds <= 8 values, its upper 8 slots repeat the lower 8."""
+def expected_image(q: np.ndarray, scales: np.ndarray, bias, k: int, compact: bool = False):
+    """The device form of a quantised weight restated on the host, per 128-class tile:
+    - fp16 image (the default): two 16 KB K-blocks of 128 rows x 128 bytes, 16-byte chunks
+      XOR-swizzled by row % 8;
+    - compact: 16 KB of bytes q + 128, 16-byte chunks of 16 K slots ordered
+      [row group r/8][K chunk s/16][row r%8].
+    K slots >= k hold q = 0 and, when the last 16-wide K step holds <= 8 values, its upper 8
+    slots repeat the lower 8. The class table holds per tile scale[128] then bias[128],
+    padded classes (0, -inf)."""
     n = q.shape[0]
     n_chunks = (n + 127) // 128
     k16 = (k + 15) // 16
     tail = k16 - 1
     merged = (k - 16 * tail) <= 8
-    vals = np.zeros((n_chunks * 128, 128), np.float16)
+    vals = np.zeros((n_chunks * 128, 128), np.int16)
     src = np.arange(128)
     if merged:
         hi = (src >= 16 * tail + 8) & (src < 16 * tail + 16)
         src = np.where(hi, src - 8, src)
     ok = src < k
-    vals[:n][:, ok] = q[:, src[ok]].astype(np.float16)
-    img = np.zeros((n_chunks, 32768), np.uint8)
-    for j in range(n_chunks * 128):
-        t, r = divmod(j, 128)
-        for s in range(128):
-            off = (s // 64) * 16384 + r * 128 + ((((s % 64) // 8) ^ (r % 8)) << 4) + (s % 8) * 2
-            img[t, off:off + 2] = np.frombuffer(vals[j, s].tobytes(), np.uint8)
-    colp = np.zeros((n_chunks * 128, 2), np.float32)
-    colp[:, 1] = -np.inf
-    colp[:n, 0] = scales
-    colp[:n, 1] = 0.0 if bias is None else bias
-    return img, colp
+    vals[:n][:, ok] = q[:, src[ok]]
+    r = np.arange(128)[:, None]
+    sl = np.arange(128)[None, :]
+    if compact:
+        img = np.zeros((n_chunks, 16384), np.uint8)
+        off = ((((r // 8) * 8 + sl // 16) * 8 + r % 8) << 4) + sl % 16
+        for t in range(n_chunks):
+            img[t, off.reshape(-1)] = (vals[t * 128:(t + 1) * 128] + 128).astype(np.uint8).reshape(-1)
+    else:
+        img = np.zeros((n_chunks, 32768), np.uint8)
+        off = (sl // 64) * 16384 + r * 128 + ((((sl % 64) // 8) ^ (r % 8)) << 4) + (sl % 8) * 2
+        for t in range(n_chunks):
+            h = vals[t * 128:(t + 1) * 128].astype(np.float16).view(np.uint8).reshape(128, 128, 2)
+            img[t, off.reshape(-1)] = h[..., 0].reshape(-1)
+            img[t, off.reshape(-1) + 1] = h[..., 1].reshape(-1)
+    sc = np.zeros(n_chunks * 128, np.float32)
+    sc[:n] = scales
+    bi = np.full(n_chunks * 128, -np.inf, np.float32)
+    bi[:n] = 0.0 if bias is None else bias
+    table = np.stack([sc.reshape(n_chunks, 128), bi.reshape(n_chunks, 128)], axis=1)
+    return img, table
 
 
+@pytest.mark.parametrize("compact", [False, True])
 @pytest.mark.parametrize("n,k", [(300, 120), (130, 123), (128, 8)])
-def test_tensor_core_image_layout(rh, ctx, oracle, n, k):
+def test_device_image_layout(rh, ctx, oracle, n, k, compact):
     rng = np.random.default_rng(5)
     w = (0.05 * rng.standard_normal((n, k))).astype(np.float32)
     b = (0.01 * rng.standard_normal(n)).astype(np.float32)
-    qw = rh.QuantizedWeight.from_f32_transposed(w, ctx=ctx, bias=b)
-    tiles, colp = qw.tensor_core_image()
+    qw = rh.QuantizedWeight.from_f32_transposed(w, ctx=ctx, bias=b, compact=compact)
+    tiles, table = qw.device_image()
     q, s = oracle.pack(w)
-    img, cp = expected_image(q, s, b, k)
+    img, tb = expected_image(q, s, b, k, compact)
     assert np.array_equal(tiles, img)
-    assert np.array_equal(colp, cp)
+    assert np.array_equal(table, tb)
+    assert np.array_equal(qw.data, q) and np.array_equal(qw.scales.view(np.uint32), s.view(np.uint32))
+
+
+def test_int8_head_device_footprint_is_at_least_3p5x_smaller(rh, ctx):
+    """src/engine/model.rs:2905-2920: INT8 must cut the live head weights by at least 3.5x
+    (head_int8 * 7 < head_fp32 * 2, with head_fp32 the transposed [18710][120] f32 copy). The
+    compact form holds only its int8 tiles and the (scale, bias) table on the device; the
+    library's own count, bias included, meets the bound. The default form keeps the fp16
+    operand image instead (faster; 1.8x smaller than FP32), the FP32 head its hi/lo images."""
+    from rust_ppocrv6_b200 import workloads
+
+    w, b = workloads.head_weights(np.random.default_rng(3))
+    qc = rh.QuantizedWeight.from_f32_transposed(w, ctx=ctx, bias=b, compact=True)
+    head_fp32 = workloads.N * workloads.K * 4
+    dev = qc.device_bytes
+    assert dev == 147 * (16384 + 1024)
+    assert dev * 7 < head_fp32 * 2, f"{dev} device bytes vs {head_fp32} FP32 bytes"
+    qw = rh.QuantizedWeight.from_f32_transposed(w, ctx=ctx, bias=b)
+    assert qw.device_bytes == 147 * (32768 + 1024)
+    fw = rh.Fp32Weight.from_f32_transposed(w, ctx=ctx, bias=b)
+    assert fw.device_bytes == 147 * (65536 + 1024)
+    for x in (qc, qw, fw):
+        x.free()
+
+
+@pytest.mark.parametrize("shape", [(18710, 120), (6906, 80), (533, 123), (129, 17)])
+def test_compact_weights_decode_bit_identically(rh, ctx, shape):
+    """The compact form feeds the tensor core the same fp16 operand values (expanded in shared
+    memory), so the fused decode, the logits and the device entry point give the same bits as
+    the default form, on the fast layouts (K=120, K=80) and the generic ones."""
+    import torch
+
+    n, k = shape
+    rng = np.random.default_rng(n + k)
+    w = (0.05 * rng.standard_normal((n, k))).astype(np.float32)
+    b = (0.01 * rng.standard_normal(n)).astype(np.float32)
+    qw = rh.QuantizedWeight.from_f32_transposed(w, ctx=ctx, bias=b)
+    qc = rh.QuantizedWeight.from_f32_transposed(w, ctx=ctx, bias=b, compact=True)
+    m = 20000 if n == 18710 else 3000
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    i0, p0 = rh.head_decode(x, qw)
+    i1, p1 = rh.head_decode(x, qc)
+    assert np.array_equal(i0, i1) and np.array_equal(p0.view(np.uint32), p1.view(np.uint32))
+    l0 = rh.matmul_quantized_b(x[:200], qw, b)
+    l1 = rh.matmul_quantized_b(x[:200], qc, b)
+    assert np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+    dx = torch.from_numpy(x).cuda()
+    di = torch.empty(m, dtype=torch.int32, device="cuda")
+    dp = torch.empty(m, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    rh.head_decode_device(qc, dx.data_ptr(), m, di.data_ptr(), dp.data_ptr())
+    ctx.sync()
+    assert np.array_equal(di.cpu().numpy(), i0)
+    qw.free()
+    qc.free()
 
 
 def test_pack_is_stream_ordered_with_pageable_input(rh, ctx, oracle):
@@ -140,11 +210,11 @@ def test_pack_is_stream_ordered_with_pageable_input(rh, ctx, oracle):
     rng = np.random.default_rng(6906)
     w = (0.05 * rng.standard_normal((6906, 80))).astype(np.float32)
     q, s = oracle.pack(w)
-    img, cp = expected_image(q, s, None, 80)
+    img, tb = expected_image(q, s, None, 80)
     for _ in range(12):
         qw = rh.QuantizedWeight.from_f32_transposed(w.copy(), ctx=ctx)
-        tiles, colp = qw.tensor_core_image()
-        assert np.array_equal(tiles, img) and np.array_equal(colp, cp)
+        tiles, table = qw.device_image()
+        assert np.array_equal(tiles, img) and np.array_equal(table, tb)
         qw.free()
 
 
