@@ -775,11 +775,12 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
     auto bar = [&](int i) -> uint32_t { return base + kOffBars + 8u * (uint32_t)i; };
     const int units = p.n_mblocks * p.n_splits;
     // ------------------------------------------------------------- epilogue
-    // Each quarter is one 32-column TMEM load; the accumulator goes back to the MMA
-    // issuer once its four quarters are loaded, and the math runs from registers. Six
-    // groups give every SM sub-partition six independent warps of softmax work; a group
-    // sees a different column subset of each row, which the online update and the merge
-    // at the end of the unit do not mind.
+    // A group takes a 64-column half of a tile: two 32-column TMEM loads, each followed by
+    // its math from registers; the accumulator goes back to the MMA issuer once both halves'
+    // second quarters are loaded. One pair of waits, releases and loop steps serves 64
+    // columns. Six groups give every SM sub-partition six independent warps of softmax work;
+    // a group sees a different column subset of each row, which the online update and the
+    // merge at the end of the unit do not mind.
     const int g = (warp - 8) >> 2;
     const int q = warp & 3;
     const int r = q * 32 + lane;
@@ -797,18 +798,18 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
         if (!__all_sync(0xffffffffu, wait_bar(bar(kBarRhoFull + (int)slot), (uc >> 2) & 1u, abort_flag, p, 6))) break;
         const float rho = rho_s[slot * 128 + r];
         const bool scaled = qflag_s[slot * 4 + q] != 0u;
-        // this group's quarters of the unit: Q = 4*(tile within the unit) + k, Q % 6 == g
-        // (numbered from each unit's start, so a row's summation order depends only on
+        // this group's halves of the unit: H = 2*(tile within the unit) + h, H % 6 == g, each
+        // the two 32-column quarters 2h, 2h+1 of its tile, loaded and processed one after the
+        // other (numbered from each unit's start, so a row's summation order depends only on
         // its unit's tile range, not on which CTA runs the unit or what it ran before).
-        const uint32_t qe = 4u * ntile;
+        const uint32_t he = 2u * ntile;
         bool first = true;
-        for (uint32_t Q = (uint32_t)g; Q < qe; Q += kEpiGroups) {
-            const uint32_t k = Q & 3u;
+        for (uint32_t H = (uint32_t)g; H < he; H += kEpiGroups) {
             // ring positions of this tile: accumulator buffer and class-table slot, with phases
-            const uint32_t cc = cc0 + (Q >> 2);
+            const uint32_t cc = cc0 + (H >> 1);
             const uint32_t buf = cc % kAccBufs, aph = (cc / kAccBufs) & 1u;
             const uint32_t cslot = cc % kCtabSlots, cph = (cc / kCtabSlots) & 1u;
-            const int c = U.c0 + (int)(Q >> 2);
+            const int c = U.c0 + (int)(H >> 1);
             if (!EMIT_LOGITS &&
                 !__all_sync(0xffffffffu, wait_bar(bar(kBarCtabFull + (int)cslot), cph, abort_flag, p, 11))) {
                 ok = false;
@@ -819,33 +820,41 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
                 break;
             }
             tc_fence_after();
-            uint32_t v[32];
-            tmem_ld32x32b_x32_wait(tmem + lane_base + kTmemAcc + buf * 128u + 32u * k, v);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarAccEmpty + (int)buf));
-            const int col0 = c * kBlockN + 32 * (int)k;
-            if (EMIT_LOGITS) {
-                const float* cp = p.ctab + (size_t)c * 256 + 32 * k;
-                float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
-                if (row < p.m) {
-                    if (scaled) logits_quarter<true>(v, cp, col0, rho, out_row, p.n);
-                    else logits_quarter<false>(v, cp, col0, rho, out_row, p.n);
+#pragma unroll
+            for (uint32_t kk = 0; kk < 2u; ++kk) {
+                const uint32_t k = 2u * (H & 1u) + kk;
+                uint32_t v[32];
+                tmem_ld32x32b_x32_wait(tmem + lane_base + kTmemAcc + buf * 128u + 32u * k, v);
+                if (kk == 1u) {  // both quarters of the half are in registers: release the accumulator
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(kBarAccEmpty + (int)buf));
                 }
-            } else {
-                const uint32_t cs = base + kOffCtab + cslot * kCtabBytes + 4u * 32u * k;
-                if (first) {
-                    if (scaled)
-                        fused_quarter<true, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
-                    else
-                        fused_quarter<false, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                const int col0 = c * kBlockN + 32 * (int)k;
+                if (EMIT_LOGITS) {
+                    const float* cp = p.ctab + (size_t)c * 256 + 32 * k;
+                    float* out_row = p.logits + (row < p.m ? row : 0) * (long long)p.n;
+                    if (row < p.m) {
+                        if (scaled) logits_quarter<true>(v, cp, col0, rho, out_row, p.n);
+                        else logits_quarter<false>(v, cp, col0, rho, out_row, p.n);
+                    }
                 } else {
-                    if (scaled)
-                        fused_quarter<true, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
-                    else
-                        fused_quarter<false, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                    const uint32_t cs = base + kOffCtab + cslot * kCtabBytes + 4u * 32u * k;
+                    if (first) {
+                        if (scaled)
+                            fused_quarter<true, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                        else
+                            fused_quarter<false, NPOLY / 2, true>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                    } else {
+                        if (scaled)
+                            fused_quarter<true, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                        else
+                            fused_quarter<false, NPOLY / 2, false>(v, cs, cs + 512u, col0, rho, rowmax, tag, st);
+                    }
+                    first = false;
                 }
-                first = false;
+            }
+            if (!EMIT_LOGITS) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kBarCtabEmpty + (int)cslot));
             }
@@ -935,7 +944,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         mbar_init(bar(kBarStageRead), 128);
         for (int i = 0; i < kAccBufs; ++i) {
             mbar_init(bar(kBarAccFull + i), 1);
-            mbar_init(bar(kBarAccEmpty + i), 16);  // one arrival per epilogue warp and quarter
+            mbar_init(bar(kBarAccEmpty + i), 8);  // one arrival per epilogue warp and half
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(kBarMFull + i), 128 * (kEpiGroups - 1));
@@ -944,7 +953,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         for (int i = 0; i < 4; ++i) {
             mbar_init(bar(kBarRhoFull + i), 128);
             mbar_init(bar(kBarCtabFull + i), 1);    // one lane of the class-table warp
-            mbar_init(bar(kBarCtabEmpty + i), 16);  // one arrival per epilogue warp and quarter
+            mbar_init(bar(kBarCtabEmpty + i), 8);  // one arrival per epilogue warp and half
             mbar_init(bar(kBarCtabRaw + i), 1);
         }
         mbar_init(bar(kBarMmaDone), 1);
