@@ -61,8 +61,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["cfg2", "cfg3", "tiny", "recpre"], default="cfg2")
-    ap.add_argument("--weights", choices=["int8", "f32"], default="int8",
-                    help="int8: the quantised head (the metric's path); f32: the engine's default FP32 head")
+    ap.add_argument("--weights", choices=["int8", "compact", "f32"], default="int8",
+                    help="int8: the quantised head with the fp16 operand image in HBM (the metric's path); "
+                         "compact: the quantised head with int8 tiles in HBM (rh_weight_pack_compact); "
+                         "f32: the engine's default FP32 head")
     ap.add_argument("--cpu-sample-lines", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-strong", action="store_true", help="skip the cfg3 strong-scaling sub-record")
@@ -343,7 +345,7 @@ def run_reference_arm(args, world, rank):
     value = srows * args.steps / dt
     sample = f"{nl} lines x T=120 ({srows} timesteps) of {desc.split(';')[0]} per step"
     print(json.dumps({
-        "impl": "reference", "metric": METRIC if args.weights == "int8" else METRIC_F32, "value": value,
+        "impl": "reference", "metric": METRIC_F32 if args.weights == "f32" else METRIC, "value": value,
         "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
         "higher_is_better": True, "scaling": "none (host CPU)", "vs_baseline": None, "dtype": "f32",
@@ -504,7 +506,7 @@ def main():
     if args.weights == "f32":
         qw = rh.Fp32Weight.from_f32_transposed(w_t, ctx=ctx, bias=bias)
     else:
-        qw = rh.QuantizedWeight.from_f32_transposed(w_t, ctx=ctx, bias=bias)
+        qw = rh.QuantizedWeight.from_f32_transposed(w_t, ctx=ctx, bias=bias, compact=args.weights == "compact")
 
     x_host = synth(rows, 1000 + rank, k_dim)
     x_bytes = x_host.nbytes
@@ -586,7 +588,7 @@ def main():
         strong = strong_record(args, world, rank, local, torch, rh, ctx, qw, barrier, max_over_ranks, host_group)
 
     out = {
-        "metric": METRIC if args.weights == "int8" else METRIC_F32, "value": value, "unit": UNIT, "n_gpus": world,
+        "metric": METRIC_F32 if args.weights == "f32" else METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "f32",
@@ -606,9 +608,12 @@ def main():
     }
     if strong is not None:
         out["strong"] = strong
-    if args.weights == "f32":
-        out["config"]["weights"] = "f32 (hi/lo fp16 images, 23 MMA K-steps per tile)"
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.weights == "int8":
+    out["config"]["weights"] = {
+        "int8": "int8 head, fp16 operand image in HBM (rh_weight_pack), %d device bytes" % qw.device_bytes,
+        "compact": "int8 head, int8 tiles in HBM expanded in shared memory (rh_weight_pack_compact), %d device bytes"
+                   % qw.device_bytes,
+        "f32": "f32 (hi/lo fp16 images, 23 MMA K-steps per tile), %d device bytes" % qw.device_bytes}[args.weights]
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.weights != "f32":
         v, threads, srows, reps, dt = cpu_reference(off, x_host, w_t, bias, args.cpu_sample_lines)
         out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                                "sample": f"{srows} timesteps ({args.cpu_sample_lines} lines of the workload) "
@@ -669,6 +674,7 @@ def strong_record(args, world, rank, local, torch, rh, ctx, qw, barrier, max_ove
         if rows:
             rh.head_decode_device(qw, xs[i % n_copies].data_ptr(), rows, d_idx.data_ptr(), d_prob.data_ptr(), sptr)
 
+    clocks = ClockSampler(local).start()
     for i in range(max(3, args.warmup)):
         dev_step(i)
     torch.cuda.synchronize()
@@ -677,11 +683,14 @@ def strong_record(args, world, rank, local, torch, rh, ctx, qw, barrier, max_ove
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    t_start = time.perf_counter()
     ev0.record(stream)
     for i in range(args.steps):
         dev_step(i)
     ev1.record(stream)
     torch.cuda.synchronize()
+    clocks.window(t_start, time.perf_counter())
+    clocks.stop()
     ctx.sync()
     dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
     barrier()
@@ -729,7 +738,7 @@ def strong_record(args, world, rank, local, torch, rh, ctx, qw, barrier, max_ove
                     f"timestep counts over {world} GPU(s)",
         "scaling": "strong", "timesteps_per_step": total, "rows_per_rank": shard_rows,
         "value": total * args.steps / (dev_ms / 1e3), "unit": UNIT, "ms_per_step": dev_ms / args.steps,
-        "l2": f"inputs rotate over {n_copies} device copies per rank",
+        "l2": f"inputs rotate over {n_copies} device copies per rank", "clocks": clocks.summary(),
         "e2e": {"value": total * args.steps / e2e_s, "unit": UNIT, "ms_per_step": e2e_s * 1e3 / args.steps,
                 "h2d_bytes_per_step": int(total * k_dim * 4), "d2h_bytes_per_step": int(total * 8),
                 "gather": "each rank: rh_head_decode_lines on its shard (pinned host memory); then idx/prob "
