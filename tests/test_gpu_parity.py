@@ -199,6 +199,12 @@ def test_compact_weights_decode_bit_identically(rh, ctx, shape):
     rh.head_decode_device(qc, dx.data_ptr(), m, di.data_ptr(), dp.data_ptr())
     ctx.sync()
     assert np.array_equal(di.cpu().numpy(), i0)
+    # the SVTR tail's [B, K, T] layout (features gathered by the same converter warps that
+    # expand the int8 tiles)
+    xt = np.ascontiguousarray(x[: (m // 40) * 40].reshape(-1, 40, k).transpose(0, 2, 1))
+    j0, q0 = rh.head_decode_kt(xt, qw)
+    j1, q1 = rh.head_decode_kt(xt, qc)
+    assert np.array_equal(j0, j1) and np.array_equal(q0.view(np.uint32), q1.view(np.uint32))
     qw.free()
     qc.free()
 
