@@ -641,6 +641,27 @@ def h2d_bandwidth(torch, src_pinned, dst, stream, reps: int = 5):
     return src_pinned.numel() * src_pinned.element_size() / (best / 1e3) / 1e9 if best else None
 
 
+def gather_shards(pack, max_rows, starts, shard_rows, rank, group, gathered, idx_all, prob_all):
+    """Collects every rank's decoded shard into rank 0's host arrays idx_all/prob_all.
+
+    `pack` (int32, 2 * max_rows) holds this rank's class indices in [0, n) and the bit patterns
+    of its probabilities in [max_rows, max_rows + n), n = shard_rows[rank]; rank r's shard
+    starts at global row starts[r]. With `group` None (one rank) the pack is unpacked in place;
+    otherwise one gather over `group` (gloo, host tensors) brings every pack to rank 0, whose
+    `gathered` holds one receive buffer per rank."""
+    if group is None:
+        gathered = [pack]
+    else:
+        import torch.distributed as dist
+
+        dist.gather(pack, gathered if rank == 0 else None, dst=0, group=group)
+    if rank != 0:
+        return
+    for r, (g0, n) in enumerate(zip(starts, shard_rows)):
+        idx_all[g0:g0 + n] = gathered[r][:n].numpy()
+        prob_all[g0:g0 + n] = gathered[r][max_rows:max_rows + n].numpy().view(np.float32)
+
+
 def strong_record(args, world, rank, local, torch, rh, ctx, qw, barrier, max_over_ranks, host_group):
     """cfg3 (one 8192-line ragged batch, ~528k timesteps) sharded over the N ranks by balanced
     timestep counts: device-resident time (max over ranks) and end to end through
@@ -704,24 +725,14 @@ def strong_record(args, world, rank, local, torch, rh, ctx, qw, barrier, max_ove
     gathered = [torch.empty(2 * max_rows, dtype=torch.int32) for _ in range(world)] if rank == 0 else None
     idx_all = np.empty(total, np.int32)
     prob_all = np.empty(total, np.float32)
+    starts = [int(off_all[a]) for a, _ in cuts]
 
     def e2e_step():
         if rows:
             rh._lib.check(lib.rh_head_decode_lines(ctx.handle, qw.handle, vp(x_pin.data_ptr()),
                                                    off.ctypes.data_as(vp), off.size - 1, k_dim,
                                                    vp(pack.data_ptr()), vp(pack.data_ptr() + 4 * max_rows)))
-        if host_group is None:
-            idx_all[:] = pack[:rows].numpy()
-            prob_all[:] = pack[max_rows:max_rows + rows].numpy().view(np.float32)
-            return
-        import torch.distributed as dist
-
-        dist.gather(pack, gathered, dst=0, group=host_group)
-        if rank == 0:
-            for r, (a, b) in enumerate(cuts):
-                g0, n = int(off_all[a]), shard_rows[r]
-                idx_all[g0:g0 + n] = gathered[r][:n].numpy()
-                prob_all[g0:g0 + n] = gathered[r][max_rows:max_rows + n].numpy().view(np.float32)
+        gather_shards(pack, max_rows, starts, shard_rows, rank, host_group, gathered, idx_all, prob_all)
 
     for _ in range(max(3, args.warmup)):
         e2e_step()

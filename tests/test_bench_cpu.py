@@ -59,6 +59,26 @@ def test_bench_helpers():
     assert np.all(np.diff(off) >= 0)
 
 
+def test_gather_shards_on_one_rank_unpacks_in_place():
+    """With one rank (no process group) the strong-scaling record's gather only unpacks its own
+    pack: idx from the front, probabilities from the bits after the padding."""
+    import torch
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    n, max_rows = 5, 7
+    idx = np.arange(n, dtype=np.int32) * 3
+    prob = np.linspace(0.25, 1.0, n, dtype=np.float32)
+    pack = torch.full((2 * max_rows,), -9, dtype=torch.int32)
+    pack[:n] = torch.from_numpy(idx)
+    pack[max_rows:max_rows + n] = torch.from_numpy(prob.view(np.int32))
+    idx_all, prob_all = np.zeros(n, np.int32), np.zeros(n, np.float32)
+    bench.gather_shards(pack, max_rows, [0], [n], 0, None, None, idx_all, prob_all)
+    np.testing.assert_array_equal(idx_all, idx)
+    np.testing.assert_array_equal(prob_all, prob)
+
+
 def test_reference_arm_for_preprocessing():
     rec = _run("--impl", "reference", "--workload", "recpre", "--steps", "1", "--warmup", "0",
                "--cpu-sample-lines", "8")

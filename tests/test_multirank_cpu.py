@@ -46,3 +46,9 @@ def test_two_gloo_ranks_shard_lines_and_agree_with_one_process(tmp_path, oracle)
     ref = oracle.head_decode(x_all, off_all, q, s, bias, threads=2)
     np.testing.assert_array_equal(idx, ref["idx"])
     np.testing.assert_array_equal(prob, ref["prob"])
+    # the benchmark's host gather rebuilt the whole batch in rank 0's arrays, bit for bit, from
+    # shards of unequal size (padding never read back)
+    assert res["shard_rows"][0] != res["shard_rows"][1]
+    np.testing.assert_array_equal(np.array(res["idx_all"], np.int32), ref["idx"])
+    np.testing.assert_array_equal(np.array(res["prob_all_bits"], np.uint32),
+                                  ref["prob"].astype(np.float32).view(np.uint32))
