@@ -1023,24 +1023,29 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         }
         const uint32_t tile_bytes = p.dual ? 2u * kTileBytes : kTileBytes;  // one fp16 stage
         const uint32_t nst = p.dual ? (uint32_t)kStagesDual : p.expand ? (uint32_t)kStages8 : (uint32_t)kStagesImage;
-        uint32_t cc = 0, uc = 0;
+        // Ring positions (weight stage s, accumulator buf) and their phase bits advance by
+        // increments and the stage descriptor by addition: this loop is the tensor core's
+        // only feed, and a division-based position costs it a dependent integer-divide
+        // sequence per tile. Adding to the descriptor's 14-bit start-address field (address
+        // / 16) cannot carry out of it: shared-window addresses stay below 256 KB.
+        const uint64_t bdesc_ring = smem_desc_k_sw128(base + kOffB);
+        const uint32_t stage_desc = tile_bytes >> 4;
+        const uint32_t a_tmem = tmem + kTmemA;
+        uint32_t s = 0, sph = 0, buf = 0, aph = 0, uc = 0;
         bool ok = true;
         for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
             const Unit U = unit_of(u, p);
             ok = __all_sync(0xffffffffu, wait_bar(bar(kBarAFull), uc & 1u, abort_flag, p, 2));
             if (!ok) break;
             tc_fence_after();
-            const uint32_t a_tmem = tmem + kTmemA;
-            for (int c = U.c0; c < U.c1; ++c, ++cc) {
-                const int s = (int)(cc % nst);
-                const uint32_t buf = cc % kAccBufs;
-                bool w = wait_bar(bar(kBarBFull + s), (cc / nst) & 1u, abort_flag, p, 3);
-                w = w && wait_bar(bar(kBarAccEmpty + (int)buf), ((cc / kAccBufs) & 1u) ^ 1u, abort_flag, p, 4);
+            for (int c = U.c0; c < U.c1; ++c) {
+                bool w = wait_bar(bar(kBarBFull + (int)s), sph, abort_flag, p, 3);
+                w = w && wait_bar(bar(kBarAccEmpty + (int)buf), aph ^ 1u, abort_flag, p, 4);
                 ok = __all_sync(0xffffffffu, w);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + kTmemAcc + buf * 128u;
-                const uint64_t bdesc0 = smem_desc_k_sw128(base + kOffB + (uint32_t)s * tile_bytes);
+                const uint64_t bdesc0 = bdesc_ring + (uint64_t)(s * stage_desc);
                 if (p.dual) {
                     if (k120) {
                         mma_tile_k120_dual_warp(d_tmem, a_tmem, bdesc0, idesc, bar(kBarBEmpty + s),
@@ -1075,6 +1080,14 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
                     }
                     mma_commit_warp(bar(kBarBEmpty + s));
                     mma_commit_warp(bar(kBarAccFull + (int)buf));
+                }
+                if (++s == nst) {
+                    s = 0u;
+                    sph ^= 1u;
+                }
+                if (++buf == (uint32_t)kAccBufs) {
+                    buf = 0u;
+                    aph ^= 1u;
                 }
             }
             if (!ok) break;
