@@ -250,66 +250,96 @@ __device__ __forceinline__ int first_in_octant(const float* t, float q) {
     return f;
 }
 
-template <bool SCALED, int NPOLY, bool FIRST>
-__device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, uint32_t es, int col0,
-                                              float rho, uint32_t rowmax, uint32_t tag, RowState& st) {
-    float t[32];
-#pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-        const float4 c4 = lds128(cs + 4u * i);
-        const float4 e4 = lds128(es + 4u * i);
-        float2 x01 = make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-        float2 x23 = make_float2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
-        if (SCALED) {
-            x01 = __fmul2_rn(x01, make_float2(rho, rho));
-            x23 = __fmul2_rn(x23, make_float2(rho, rho));
-        }
-        const float2 t01 = __ffma2_rn(x01, make_float2(c4.x, c4.y), make_float2(e4.x, e4.y));
-        const float2 t23 = __ffma2_rn(x23, make_float2(c4.z, c4.w), make_float2(e4.z, e4.w));
-        t[i] = t01.x;
-        t[i + 1] = t01.y;
-        t[i + 2] = t23.x;
-        t[i + 3] = t23.y;
+// t = D*c + e for four columns i..i+3 (the class table entries are warp-uniform broadcast
+// loads from shared memory).
+template <bool SCALED>
+__device__ __forceinline__ void quarter_t4(const uint32_t* v, uint32_t cs, uint32_t es, float rho, int i, float* t) {
+    const float4 c4 = lds128(cs + 4u * i);
+    const float4 e4 = lds128(es + 4u * i);
+    float2 x01 = make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+    float2 x23 = make_float2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+    if (SCALED) {
+        x01 = __fmul2_rn(x01, make_float2(rho, rho));
+        x23 = __fmul2_rn(x23, make_float2(rho, rho));
     }
-    // max over the quarter through the maxima of its four 8-column octants (kept for the
-    // first-argmax search, which then scans one octant instead of 32 columns)
-    float oct[4];
+    const float2 t01 = __ffma2_rn(x01, make_float2(c4.x, c4.y), make_float2(e4.x, e4.y));
+    const float2 t23 = __ffma2_rn(x23, make_float2(c4.z, c4.w), make_float2(e4.z, e4.w));
+    t[i] = t01.x;
+    t[i + 1] = t01.y;
+    t[i + 2] = t23.x;
+    t[i + 3] = t23.y;
+}
+
+// 2^(t[i] - off), 2^(t[i+1] - off) (off = 0: no subtraction) added to acc; pairs below
+// NPOLY go to the FMA-pipe polynomial instead of the MUFU.
+template <int NPOLY, bool REL>
+__device__ __forceinline__ void quarter_exp2(const float* t, int i, float2 nm, float2& acc) {
+    float2 x = make_float2(t[i], t[i + 1]);
+    if (REL) x = __fadd2_rn(x, nm);
+    float2 e;
+    if ((i >> 1) < NPOLY)
+        e = exp2_poly2(x);
+    else
+        e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+    acc = __fadd2_rn(acc, e);
+}
+
+// Maxima of the quarter's four 8-column octants (kept for the first-argmax search, which then
+// scans one octant instead of 32 columns).
+__device__ __forceinline__ void quarter_octants(const float* t, float* oct) {
 #pragma unroll
     for (int j = 0; j < 4; ++j)
         oct[j] = max3f(max3f(t[8 * j], t[8 * j + 1], t[8 * j + 2]), max3f(t[8 * j + 3], t[8 * j + 4], t[8 * j + 5]),
                        fmaxf(t[8 * j + 6], t[8 * j + 7]));
-    const float qmax = max3f(oct[0], oct[1], fmaxf(oct[2], oct[3]));
-    if constexpr (FIRST) {  // first columns of this row in the unit: pick the mode
+}
+
+// The t values, their exps and the octant maxima of a quarter whose offset is already known,
+// as one straight-line block: the compiler can then interleave the MUFU exps with the shared
+// loads, FMAs and max tree, so each warp keeps the MUFU fed instead of alternating an
+// ALU phase with a burst of 32 exps.
+template <bool SCALED, int NPOLY, bool REL>
+__device__ __forceinline__ void quarter_known_offset(const uint32_t* v, uint32_t cs, uint32_t es, float rho, float off,
+                                                     float* t, float* oct, float2& acc) {
+    const float2 nm = make_float2(-off, -off);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+        quarter_t4<SCALED>(v, cs, es, rho, i, t);
+        quarter_exp2<NPOLY, REL>(t, i, nm, acc);
+        quarter_exp2<NPOLY, REL>(t, i + 2, nm, acc);
+    }
+    quarter_octants(t, oct);
+}
+
+template <bool SCALED, int NPOLY, bool FIRST>
+__device__ __forceinline__ void fused_quarter(const uint32_t* v, uint32_t cs, uint32_t es, int col0,
+                                              float rho, uint32_t rowmax, uint32_t tag, RowState& st) {
+    float t[32];
+    float oct[4];
+    float2 acc = make_float2(0.f, 0.f);
+    float qmax;
+    if constexpr (FIRST) {  // first columns of this row in the unit: the max picks the mode
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) quarter_t4<SCALED>(v, cs, es, rho, i, t);
+        quarter_octants(t, oct);
+        qmax = max3f(oct[0], oct[1], fmaxf(oct[2], oct[3]));
         // (no early return for padded-only columns: every lane reaches the warp votes below)
         st.off = qmax == -CUDART_INF_F ? -CUDART_INF_F : (qmax >= kAbsLo && qmax <= kAbsHi) ? 0.0f : qmax;
-    }
-    // The offset is known before this quarter, so the exps need not wait for the max tree
-    // and both run interleaved. A warp whose rows are all in the absolute mode skips the
-    // per-column subtraction.
-    float2 acc = make_float2(0.f, 0.f);
-    if (__all_sync(0xffffffffu, st.off == 0.0f)) {
+        const float2 nm = make_float2(-st.off, -st.off);
+        if (__all_sync(0xffffffffu, st.off == 0.0f)) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-            const float2 x = make_float2(t[i], t[i + 1]);
-            float2 e;
-            if ((i >> 1) < NPOLY)
-                e = exp2_poly2(x);
-            else
-                e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-            acc = __fadd2_rn(acc, e);
+            for (int i = 0; i < 32; i += 2) quarter_exp2<NPOLY, false>(t, i, nm, acc);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) quarter_exp2<NPOLY, true>(t, i, nm, acc);
         }
     } else {
-        const float2 nm = make_float2(-st.off, -st.off);
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-            const float2 x = __fadd2_rn(make_float2(t[i], t[i + 1]), nm);
-            float2 e;
-            if ((i >> 1) < NPOLY)
-                e = exp2_poly2(x);
-            else
-                e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-            acc = __fadd2_rn(acc, e);
-        }
+        // The offset is known before this quarter, so the exps need not wait for the max
+        // tree. A warp whose rows are all in the absolute mode skips the per-column subtraction.
+        if (__all_sync(0xffffffffu, st.off == 0.0f))
+            quarter_known_offset<SCALED, NPOLY, false>(v, cs, es, rho, 0.0f, t, oct, acc);
+        else
+            quarter_known_offset<SCALED, NPOLY, true>(v, cs, es, rho, st.off, t, oct, acc);
+        qmax = max3f(oct[0], oct[1], fmaxf(oct[2], oct[3]));
     }
     float sq = acc.x + acc.y;
     // absolute mode: leave it only if the max passes kAbsHi; relative mode: rescale on a rise
