@@ -937,13 +937,13 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
 // -------------------------------------------------------------------- head
 // Warp roles (one CTA per SM, persistent over work units = (row block, class range)):
 //   warp 0      lane 0: weight-tile producer (TMA bulk copies into the smem ring)
-//   warp 1      TMEM allocator; lane 0: MMA issuer
+//   warp 1      TMEM allocator; elected lane: MMA issuer
 //   warp 2      lane 0 (fused variant): class-table producer (TMA bulk copies, 4-slot ring)
 //   warp 3      idle
 //   warps 4-7   A converters: f32 rows -> (hi, lo) fp16 parts in TMEM, one lane quadrant each
-//   warps 8-31  epilogue groups 0-5 (4 warps each, lane quadrants 0-3); the 32-column
-//               quarters of a unit's accumulator tiles, numbered in order from the unit's
-//               start, go round-robin to the groups: group g takes quarters g, g+6, ...
+//   warps 8-31  epilogue groups 0-5 (4 warps each, lane quadrants 0-3); the 64-column
+//               halves of a unit's accumulator tiles, numbered in order from the unit's
+//               start, go round-robin to the groups: group g takes halves g, g+6, ...
 template <bool EMIT_LOGITS, int NPOLY>
 __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_constant__ HeadParams p) {
     extern __shared__ uint8_t smem_raw[];

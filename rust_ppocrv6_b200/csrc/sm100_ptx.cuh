@@ -109,56 +109,36 @@ __device__ __forceinline__ void mma_commit_warp(uint32_t bar) {
 // K columns 16kc..16kc+15 sit in K-block kc/4 (16 KB apart) at 32 B x (kc % 4).
 __device__ __forceinline__ void mma_tile_k120_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                                    uint32_t bar_b_empty, uint32_t bar_acc_full) {
+    // The low-part steps read the same B slices as high-part steps 0..6, so the tile needs 8
+    // descriptors; the A operand's K-steps are immediate column offsets of its TMEM address.
     asm volatile(
-        "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 b<15>;\n\t.reg .b32 a<15>;\n\t"
+        "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 b<8>;\n\t"
         "elect.sync _|e, 0xffffffff;\n\t"
         "setp.ne.b32 pf, 0, 0;\n\t"
         "setp.eq.b32 pt, 0, 0;\n\t"
-        "add.s64 b0, %2, 0;\n\t"
-        "add.u32 a0, %1, 0;\n\t"
+        "mov.b64 b0, %2;\n\t"
         "add.s64 b1, %2, 2;\n\t"
-        "add.u32 a1, %1, 8;\n\t"
         "add.s64 b2, %2, 4;\n\t"
-        "add.u32 a2, %1, 16;\n\t"
         "add.s64 b3, %2, 6;\n\t"
-        "add.u32 a3, %1, 24;\n\t"
         "add.s64 b4, %2, 1024;\n\t"
-        "add.u32 a4, %1, 32;\n\t"
         "add.s64 b5, %2, 1026;\n\t"
-        "add.u32 a5, %1, 40;\n\t"
         "add.s64 b6, %2, 1028;\n\t"
-        "add.u32 a6, %1, 48;\n\t"
         "add.s64 b7, %2, 1030;\n\t"
-        "add.u32 a7, %1, 56;\n\t"
-        "add.s64 b8, %2, 0;\n\t"
-        "add.u32 a8, %1, 64;\n\t"
-        "add.s64 b9, %2, 2;\n\t"
-        "add.u32 a9, %1, 72;\n\t"
-        "add.s64 b10, %2, 4;\n\t"
-        "add.u32 a10, %1, 80;\n\t"
-        "add.s64 b11, %2, 6;\n\t"
-        "add.u32 a11, %1, 88;\n\t"
-        "add.s64 b12, %2, 1024;\n\t"
-        "add.u32 a12, %1, 96;\n\t"
-        "add.s64 b13, %2, 1026;\n\t"
-        "add.u32 a13, %1, 104;\n\t"
-        "add.s64 b14, %2, 1028;\n\t"
-        "add.u32 a14, %1, 112;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a0], b0, %3, pf;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], b4, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], b5, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], b6, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], b7, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a8], b8, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a9], b9, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a10], b10, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a11], b11, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a12], b12, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a13], b13, %3, pt;\n\t"
-        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a14], b14, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], b0, %3, pf;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+8], b1, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+16], b2, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+24], b3, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+32], b4, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+40], b5, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+48], b6, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+56], b7, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+64], b0, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+72], b1, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+80], b2, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+88], b3, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+96], b4, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+104], b5, %3, pt;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1+112], b6, %3, pt;\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%4];\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
         ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(bar_b_empty), "r"(bar_acc_full)
