@@ -840,14 +840,20 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
             const uint32_t buf = cc % kAccBufs, aph = (cc / kAccBufs) & 1u;
             const uint32_t cslot = cc % kCtabSlots, cph = (cc / kCtabSlots) & 1u;
             const int c = U.c0 + (int)(H >> 1);
-            if (!EMIT_LOGITS &&
-                !__all_sync(0xffffffffu, wait_bar(bar(kBarCtabFull + (int)cslot), cph, abort_flag, p, 11))) {
-                ok = false;
-                break;
-            }
-            if (!__all_sync(0xffffffffu, wait_bar(bar(kBarAccFull + (int)buf), aph, abort_flag, p, 7))) {
-                ok = false;
-                break;
+            // both waits at once on the common path (class table and accumulator ready)
+            const bool ready = EMIT_LOGITS ? mbar_try_wait(bar(kBarAccFull + (int)buf), aph)
+                                           : mbar_try_wait2(bar(kBarCtabFull + (int)cslot), cph,
+                                                            bar(kBarAccFull + (int)buf), aph);
+            if (!__all_sync(0xffffffffu, ready)) {
+                if (!EMIT_LOGITS &&
+                    !__all_sync(0xffffffffu, wait_bar(bar(kBarCtabFull + (int)cslot), cph, abort_flag, p, 11))) {
+                    ok = false;
+                    break;
+                }
+                if (!__all_sync(0xffffffffu, wait_bar(bar(kBarAccFull + (int)buf), aph, abort_flag, p, 7))) {
+                    ok = false;
+                    break;
+                }
             }
             tc_fence_after();
 #pragma unroll
@@ -1069,8 +1075,12 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
             if (!ok) break;
             tc_fence_after();
             for (int c = U.c0; c < U.c1; ++c) {
-                bool w = wait_bar(bar(kBarBFull + (int)s), sph, abort_flag, p, 3);
-                w = w && wait_bar(bar(kBarAccEmpty + (int)buf), aph ^ 1u, abort_flag, p, 4);
+                // both waits at once on the common path (stage and accumulator ready)
+                bool w = mbar_try_wait2(bar(kBarBFull + (int)s), sph, bar(kBarAccEmpty + (int)buf), aph ^ 1u);
+                if (!__all_sync(0xffffffffu, w)) {
+                    w = wait_bar(bar(kBarBFull + (int)s), sph, abort_flag, p, 3);
+                    w = w && wait_bar(bar(kBarAccEmpty + (int)buf), aph ^ 1u, abort_flag, p, 4);
+                }
                 ok = __all_sync(0xffffffffu, w);
                 if (!ok) break;
                 tc_fence_after();

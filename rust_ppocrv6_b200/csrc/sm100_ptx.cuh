@@ -34,6 +34,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Both barriers' phases complete? The two try_waits issue back to back, so their latencies
+// overlap (two waits in a row on the hot path, where both have usually passed already).
+__device__ __forceinline__ bool mbar_try_wait2(uint32_t bar0, uint32_t parity0, uint32_t bar1, uint32_t parity1) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p0, p1;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p0, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p1, [%3], %4;\n\t"
+        "and.pred p0, p0, p1;\n\t"
+        "selp.u32 %0, 1, 0, p0;\n\t}"
+        : "=r"(ok)
+        : "r"(bar0), "r"(parity0), "r"(bar1), "r"(parity1)
+        : "memory");
+    return ok != 0;
+}
 // try_wait that may suspend the thread for up to `hint_ns` (or until the phase completes)
 // instead of returning at once, so waiting warps do not take issue slots from working ones.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
