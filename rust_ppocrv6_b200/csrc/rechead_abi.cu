@@ -63,6 +63,7 @@ struct Slot {
     cudaStream_t copy_stream = nullptr;  // host-to-device copies that overlap the kernels
     cudaEvent_t copied = nullptr;
     int* d_status = nullptr;
+    int* h_status = nullptr;  // pinned copy of d_status, read back at the end of a call
     DevBuf a, idx, prob, out, partial;
     DevBuf lines, tok_off, tokens, scores;  // CTC collapse on the device
     DevBuf pre_rgb, pre_lines, pre_coords, pre_wts, pre_out;  // recognition preprocessing
@@ -79,6 +80,7 @@ struct Slot {
                           &pre_coords, &pre_wts, &pre_out})
             b->release();
         if (d_status) cudaFree(d_status);
+        if (h_status) cudaFreeHost(h_status);
         if (copied) cudaEventDestroy(copied);
         if (pre_done) cudaEventDestroy(pre_done);
         if (part_done) cudaEventDestroy(part_done);
@@ -262,10 +264,8 @@ int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per&
     return RH_OK;
 }
 
-int read_status(Slot& s) {
-    int st[2] = {0, 0};
-    RH_CUDA(cudaMemcpyAsync(st, s.d_status, sizeof(st), cudaMemcpyDeviceToHost, s.stream));
-    RH_CUDA(cudaStreamSynchronize(s.stream));
+// A non-zero device status word `st` (copied back from s.d_status) as an error; clears it.
+int status_error(Slot& s, const int* st) {
     if (st[0] != 0) {
         RH_CUDA(cudaMemsetAsync(s.d_status, 0, 2 * sizeof(int), s.stream));
         RH_CUDA(cudaStreamSynchronize(s.stream));
@@ -275,6 +275,22 @@ int read_status(Slot& s) {
         return fail(RH_ERR_CUDA, "device status " + std::to_string(st[0]));
     }
     return RH_OK;
+}
+
+int read_status(Slot& s) {
+    int st[2] = {0, 0};
+    RH_CUDA(cudaMemcpyAsync(st, s.d_status, sizeof(st), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    return status_error(s, st);
+}
+
+// Waits for the work queued on the slot's stream and checks the device status, whose copy back
+// is queued on the same stream first: one synchronisation at the end of a call, not two.
+int sync_and_check(Slot& s) {
+    RH_CUDA(cudaMemcpyAsync(s.h_status, s.d_status, 2 * sizeof(int), cudaMemcpyDeviceToHost, s.stream));
+    RH_CUDA(cudaStreamSynchronize(s.stream));
+    const int st[2] = {s.h_status[0], s.h_status[1]};
+    return status_error(s, st);
 }
 
 const rh_weight::Per* weight_on(const rh_weight* w, int device) {
@@ -336,8 +352,7 @@ int run_host_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, 
     Slot& s = *ctx->slots[slot];
     std::lock_guard<std::mutex> lock(s.mu);
     if (int rc = host_pass_locked(ctx, w, s, a, rows, idx, prob, logits)) return rc;
-    RH_CUDA(cudaStreamSynchronize(s.stream));
-    return read_status(s);
+    return sync_and_check(s);
 }
 
 // The fused head then the CTC collapse on one device for lines [0, n_lines) of a shard whose
@@ -368,8 +383,7 @@ int run_ctc_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* a, c
     RH_CUDA(cudaMemcpyAsync(token_offsets, s.tok_off.p, off_bytes, cudaMemcpyDeviceToHost, s.stream));
     if (n_lines > 0)
         RH_CUDA(cudaMemcpyAsync(scores, s.scores.p, (size_t)n_lines * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
-    RH_CUDA(cudaStreamSynchronize(s.stream));
-    if (int rc = read_status(s)) return rc;
+    if (int rc = sync_and_check(s)) return rc;
     const int64_t n_tok = token_offsets[n_lines];
     if (n_tok < 0 || n_tok > rows) return fail(RH_ERR_CUDA, "CTC collapse produced an impossible token count");
     if (n_tok > 0) {
@@ -492,8 +506,7 @@ int kt_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* x, int64_
         return rc;
     RH_CUDA(cudaMemcpyAsync(idx, s.idx.p, (size_t)rows * sizeof(int32_t), cudaMemcpyDeviceToHost, s.stream));
     RH_CUDA(cudaMemcpyAsync(prob, s.prob.p, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
-    RH_CUDA(cudaStreamSynchronize(s.stream));
-    return read_status(s);
+    return sync_and_check(s);
 }
 
 // The head and the GPU collapse of `nb` padded lines (line b valid for valid_t[b] <= t_len
@@ -543,8 +556,7 @@ int kt_ctc_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* x, in
     RH_CUDA(cudaMemcpyAsync(token_offsets, s.tok_off.p, (size_t)(nb + 1) * sizeof(int64_t), cudaMemcpyDeviceToHost,
                             s.stream));
     RH_CUDA(cudaMemcpyAsync(scores, s.scores.p, (size_t)nb * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
-    RH_CUDA(cudaStreamSynchronize(s.stream));
-    if (int rc = read_status(s)) return rc;
+    if (int rc = sync_and_check(s)) return rc;
     const int64_t n_tok = token_offsets[nb];
     if (n_tok < 0 || n_tok > total) return fail(RH_ERR_CUDA, "CTC collapse produced an impossible token count");
     if (n_tok > 0) {
@@ -761,8 +773,7 @@ int rec_host_on_slot(rh_ctx* ctx, int slot, const uint8_t* rgb, const int64_t* o
                                 (size_t)pn * line_floats * sizeof(float), cudaMemcpyDeviceToHost, s.stream));
     }
     RH_CUDA(cudaEventRecord(s.pre_done, s.stream));
-    RH_CUDA(cudaStreamSynchronize(s.stream));
-    return read_status(s);
+    return sync_and_check(s);
 }
 
 }  // namespace
@@ -814,6 +825,7 @@ int rh_ctx_create(const int* devices, int n_devices, rh_ctx** out) {
         RH_CUDA(cudaStreamCreateWithFlags(&s->copy_stream, cudaStreamNonBlocking));
         RH_CUDA(cudaEventCreateWithFlags(&s->copied, cudaEventDisableTiming));
         RH_CUDA(cudaMalloc(&s->d_status, 2 * sizeof(int)));
+        RH_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->h_status), 2 * sizeof(int), cudaHostAllocDefault));
         RH_CUDA(cudaMemsetAsync(s->d_status, 0, 2 * sizeof(int), s->stream));
         RH_CUDA(cudaStreamSynchronize(s->stream));
         ctx->slots.push_back(std::move(s));
