@@ -834,12 +834,18 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
         // its unit's tile range, not on which CTA runs the unit or what it ran before).
         const uint32_t he = 2u * ntile;
         bool first = true;
-        for (uint32_t H = (uint32_t)g; H < he; H += kEpiGroups) {
-            // ring positions of this tile: accumulator buffer and class-table slot, with phases
-            const uint32_t cc = cc0 + (H >> 1);
-            const uint32_t buf = cc % kAccBufs, aph = (cc / kAccBufs) & 1u;
-            const uint32_t cslot = cc % kCtabSlots, cph = (cc / kCtabSlots) & 1u;
-            const int c = U.c0 + (int)(H >> 1);
+        // Ring positions of this group's first tile in the unit (accumulator buffer and
+        // class-table slot, with their phases); the group's next half lies kEpiGroups / 2 = 3
+        // tiles further, so they then advance by increments: the buffer stays (3 buffers) and
+        // its phase flips, the slot moves 3 on (4 slots) and its phase flips when it wraps.
+        static_assert(kEpiGroups == 6 && kAccBufs == 3 && kCtabSlots == 4, "ring advance per half below");
+        uint32_t cc = cc0 + ((uint32_t)g >> 1);
+        const uint32_t buf = cc % kAccBufs;
+        uint32_t aph = (cc / kAccBufs) & 1u;
+        uint32_t cslot = cc % kCtabSlots, cph = (cc / kCtabSlots) & 1u;
+        int c = U.c0 + (g >> 1);
+        for (uint32_t H = (uint32_t)g; H < he;
+             H += kEpiGroups, cc += 3u, c += 3, aph ^= 1u, cph ^= (cslot != 0u) ? 1u : 0u, cslot = (cslot + 3u) & 3u) {
             // both waits at once on the common path (class table and accumulator ready)
             const bool ready = EMIT_LOGITS ? mbar_try_wait(bar(kBarAccFull + (int)buf), aph)
                                            : mbar_try_wait2(bar(kBarCtabFull + (int)cslot), cph,
