@@ -195,8 +195,9 @@ int rh_matmul_quantized_b_device(rh_ctx *ctx, const rh_weight *w, int slot, cons
  * Its only scratch (the per-split partial rows that the class-range split writes and the
  * merge kernel reads) is a fixed 4 MiB array in the library's device image, so every GPU that
  * uses the library holds those 4 MiB until the process exits. Limit: at most 262,144
- * timestep rows per call (larger calls fail with RH_ERR_INVALID_ARG and launch nothing);
- * the class-range split is coarsened when splits x rows would not fit.
+ * timestep rows per call (larger calls fail with RH_ERR_INVALID_ARG and launch nothing); only
+ * the row blocks after the last full wave are split, so a call needs at most about one wave's
+ * rows (148 x 128) of partial entries whatever its size.
  *  - The first call on a device resolves the array's device address (cudaGetSymbolAddress,
  *    which may load the library's device code); make that first call before any stream
  *    capture.

@@ -64,11 +64,14 @@ struct HeadParams {
     int expand;                // int8 tiles, expanded to fp16 in shared memory by warps 4-7
     const float* ctab;         // n_chunks * 256: per tile scale[128] then bias[128]; padded classes (0, -inf)
     int n_mblocks;             // ceil(m / 128)
-    int n_splits;              // class-range splits per row block
+    int whole_units;           // row blocks [0, whole_units) are units of the whole class range (full
+                               // waves of the grid, no merge); the rest are split as below
+    int n_splits;              // class-range splits per row block from whole_units on
     int chunks_per_split;
     int32_t* idx;              // fused, n_splits == 1: argmax class per row
     float* prob;               // fused, n_splits == 1: max softmax probability per row
-    float4* partial;           // fused, n_splits > 1: [n_splits][m] (max, sum, idx bits, 0), log2 units
+    float4* partial;           // fused, n_splits > 1: [n_splits][m - 128 whole_units] (max, sum, idx bits,
+                               // 0) of the split row blocks' rows, log2 units
     float* logits;             // logits variant: [m][n]
     int* status;               // [2]
     unsigned long long timeout_ns;

@@ -105,17 +105,24 @@ Geometry geometry(int64_t n, int64_t k) {
     return g;
 }
 
-// Chooses how many class-range splits each 128-row block gets so that the persistent grid
-// is evenly loaded: cost = waves * (chunks per unit + per-unit overhead).
-void plan(int64_t m, int n_chunks, int sms, int& n_mblocks, int& n_splits, int& cps, int& grid) {
+// Chooses the work units of a launch. As many full waves of whole row blocks (the whole class
+// range, no merge) as the row blocks fill, then the remaining row blocks (fewer than the grid)
+// split into as many class ranges as keep their last wave evenly loaded: cost = waves * (chunks
+// per unit + per-unit overhead). Whole row blocks keep the number of units per CTA, and so of
+// A-operand hand-overs between units, at its least (cfg2: 7 units per CTA instead of 13 with
+// every row block split in two).
+void plan(int64_t m, int n_chunks, int sms, int& n_mblocks, int& whole_units, int& n_splits, int& cps,
+          int& grid) {
     n_mblocks = (int)((m + rh::kBlockM - 1) / rh::kBlockM);
+    whole_units = (n_mblocks / sms) * sms;
+    const int rest = n_mblocks - whole_units;
     double best = 1e300;
     n_splits = 1;
     cps = n_chunks;
-    for (int s = 1; s <= n_chunks; ++s) {
+    for (int s = 1; rest > 0 && s <= n_chunks; ++s) {
         const int c = (n_chunks + s - 1) / s;
         const int s_eff = (n_chunks + c - 1) / c;
-        const long long units = (long long)n_mblocks * s_eff;
+        const long long units = (long long)rest * s_eff;
         const long long waves = (units + sms - 1) / sms;
         const double cost = (double)waves * (c + 2.0);
         if (cost < best - 1e-9) {
@@ -124,8 +131,14 @@ void plan(int64_t m, int n_chunks, int sms, int& n_mblocks, int& n_splits, int& 
             cps = c;
         }
     }
-    const long long units = (long long)n_mblocks * n_splits;
+    const long long units = (long long)whole_units + (long long)rest * n_splits;
     grid = (int)std::min<long long>(units, sms);
+}
+
+// Rows whose idx/prob come through the split merge: those of the row blocks after the whole
+// units, when they are split.
+int64_t split_rows(const rh::HeadParams& p) {
+    return p.n_splits > 1 ? p.m - (int64_t)p.whole_units * rh::kBlockM : 0;
 }
 
 std::vector<int> injected_fault_slots() {
@@ -197,8 +210,8 @@ int check_ctx(rh_ctx* ctx) {
 // its split scratch. Every head launch path builds its parameters here.
 rh::HeadParams head_params(rh_ctx* ctx, const rh_weight* w, const Slot& s, const rh_weight::Per& pw, const float* d_a,
                            int64_t rows, int64_t a_t, int32_t* d_idx, float* d_prob, float* d_logits, int& grid) {
-    int n_mblocks, n_splits, cps;
-    plan(rows, w->g.n_chunks, s.sms, n_mblocks, n_splits, cps, grid);
+    int n_mblocks, whole_units, n_splits, cps;
+    plan(rows, w->g.n_chunks, s.sms, n_mblocks, whole_units, n_splits, cps, grid);
     rh::HeadParams p{};
     p.a = d_a;
     p.a_t = a_t;
@@ -215,6 +228,7 @@ rh::HeadParams head_params(rh_ctx* ctx, const rh_weight* w, const Slot& s, const
     p.ctab = pw.ctab;
     p.poly_pairs = poly_pairs_setting();
     p.n_mblocks = n_mblocks;
+    p.whole_units = whole_units;
     p.n_splits = n_splits;
     p.chunks_per_split = cps;
     p.idx = d_idx;
@@ -229,12 +243,13 @@ rh::HeadParams head_params(rh_ctx* ctx, const rh_weight* w, const Slot& s, const
 }
 
 // Launches the head, then (fused, class range split) the merge of the per-split partials in
-// p.partial, on `stream`.
+// p.partial over the split row blocks' rows, on `stream`.
 int launch_head_and_merge(Slot& s, const rh::HeadParams& p, bool emit_logits, int grid, cudaStream_t stream) {
     RH_CUDA(rh::launch_head(p, emit_logits, grid, stream));
     s.launches++;
-    if (!emit_logits && p.n_splits > 1) {
-        RH_CUDA(rh::launch_merge(p.partial, p.n_splits, p.m, p.idx, p.prob, stream));
+    if (!emit_logits && split_rows(p) > 0) {
+        const int64_t row0 = (int64_t)p.whole_units * rh::kBlockM;
+        RH_CUDA(rh::launch_merge(p.partial, p.n_splits, split_rows(p), p.idx + row0, p.prob + row0, stream));
         s.launches++;
     }
     return RH_OK;
@@ -247,13 +262,13 @@ int enqueue_head(rh_ctx* ctx, const rh_weight* w, Slot& s, const rh_weight::Per&
     if (rows <= 0) return RH_OK;
     int grid;
     rh::HeadParams p = head_params(ctx, w, s, pw, d_a, rows, a_t, d_idx, d_prob, d_logits, grid);
-    const bool split = !emit_logits && p.n_splits > 1;
+    const bool split = !emit_logits && split_rows(p) > 0;
     if (split) {
         // The split scratch is the slot's: order this call after the previous merge that read
         // it (which may run on another caller stream), and let that merge finish before the
         // buffer is reallocated.
         if (!s.part_done) RH_CUDA(cudaEventCreateWithFlags(&s.part_done, cudaEventDisableTiming));
-        const size_t need = (size_t)p.n_splits * (size_t)rows * sizeof(float4);
+        const size_t need = (size_t)p.n_splits * (size_t)split_rows(p) * sizeof(float4);
         if (need > s.partial.cap) RH_CUDA(cudaEventSynchronize(s.part_done));
         RH_CUDA(s.partial.ensure(need));
         RH_CUDA(cudaStreamWaitEvent(stream, s.part_done, 0));
@@ -1351,15 +1366,14 @@ int rh_head_decode_device_noalloc(rh_ctx* ctx, const rh_weight* w, int slot, con
 
     int grid;
     rh::HeadParams p = head_params(ctx, w, s, *pw, d_a, rows, 0, d_idx, d_prob, nullptr, grid);
-    if (p.n_splits > 1 && (int64_t)p.n_splits * rows > kNoAllocScratchEntries) {
-        // fewer, longer class ranges so that splits x rows partial entries fit the array
-        const int max_splits = (int)(kNoAllocScratchEntries / rows);
-        const int cps = max_splits <= 1 ? w->g.n_chunks : (w->g.n_chunks + max_splits - 1) / max_splits;
-        p.chunks_per_split = cps;
-        p.n_splits = (w->g.n_chunks + cps - 1) / cps;
-        grid = (int)std::min<long long>((long long)p.n_mblocks * p.n_splits, s.sms);
-    }
-    p.partial = p.n_splits > 1 ? scratch : nullptr;
+    // Partial entries: splits x the rows of the split row blocks, which are fewer than one
+    // wave (148 x 128 rows); the planner keeps splits x those blocks near one wave, so the
+    // plan fits the array at any call size. The check only guards that.
+    const int64_t entries = (int64_t)p.n_splits * split_rows(p);
+    if (entries > kNoAllocScratchEntries)
+        return fail(RH_ERR_UNSUPPORTED, "rh_head_decode_device_noalloc: the work plan needs " + std::to_string(entries) +
+                                            " partial entries, more than its static array holds");
+    p.partial = split_rows(p) > 0 ? scratch : nullptr;
     return launch_head_and_merge(s, p, false, grid, (cudaStream_t)stream);
 }
 

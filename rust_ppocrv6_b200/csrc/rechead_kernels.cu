@@ -94,10 +94,28 @@ struct Unit {
     int mb, sp, c0, c1;
 };
 
+// Units: row blocks [0, whole_units) with the whole class range (unit u = row block u; the
+// plan makes whole_units a multiple of the grid, so they fill whole waves in row-block order),
+// then every later row block split into n_splits class ranges (unit whole_units + v = split
+// v % n_splits of row block whole_units + v / n_splits). A CTA takes units blockIdx.x,
+// blockIdx.x + gridDim.x, ...
+__device__ __forceinline__ bool unit_exists(int u, const HeadParams& p) {
+    return u < p.whole_units + (p.n_mblocks - p.whole_units) * p.n_splits;
+}
+
 __device__ __forceinline__ Unit unit_of(int u, const HeadParams& p) {
     Unit U;
-    U.mb = u / p.n_splits;
-    U.sp = u - U.mb * p.n_splits;
+    if (u < p.whole_units) {
+        U.mb = u;
+        U.sp = 0;
+        U.c0 = 0;
+        U.c1 = p.n_chunks;
+        return U;
+    }
+    const int v = u - p.whole_units;
+    const int blk = v / p.n_splits;
+    U.mb = p.whole_units + blk;
+    U.sp = v - blk * p.n_splits;
     U.c0 = U.sp * p.chunks_per_split;
     U.c1 = min(U.c0 + p.chunks_per_split, p.n_chunks);
     return U;
@@ -604,7 +622,6 @@ __device__ __noinline__ void converter_warps(const HeadParams& p, uint32_t base,
     float* rho_s = reinterpret_cast<float*>(gbase + kOffRho);
     uint32_t* qflag_s = reinterpret_cast<uint32_t*>(gbase + kOffQFlag);
     auto bar = [&](int i) -> uint32_t { return base + kOffBars + 8u * (uint32_t)i; };
-    const int units = p.n_mblocks * p.n_splits;
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
@@ -639,11 +656,11 @@ __device__ __noinline__ void converter_warps(const HeadParams& p, uint32_t base,
         for (int kk = 0; kk < p.k; ++kk) my_stage[kk] = __ldg(src + (long long)kk * p.a_t);
     };
     uint32_t staged_issued = 0, staged_used = 0;
-    if (bulk && r == 0 && (int)blockIdx.x < units) {
+    if (bulk && r == 0 && unit_exists(blockIdx.x, p)) {
         issue_stage(blockIdx.x);
         staged_issued = 1;
     }
-    if (staged && kt && (int)blockIdx.x < units) gather_row(blockIdx.x);
+    if (staged && kt && unit_exists(blockIdx.x, p)) gather_row(blockIdx.x);
     const long long astride = kt ? p.a_t : 1;
     // A operand of unit u (the uc-th unit of this CTA) into TMEM; false when a wait gave up
     // (the caller then leaves its loop as a whole warp).
@@ -748,9 +765,9 @@ __device__ __noinline__ void converter_warps(const HeadParams& p, uint32_t base,
         mbar_arrive(bar(kBarAFull));
         mbar_arrive(bar(kBarRhoFull + (int)slot));
         // next unit's rows into the staging buffer once every converter has read this one
-        if (staged && kt && u + (int)gridDim.x < units) gather_row(u + (int)gridDim.x);
+        if (staged && kt && unit_exists(u + (int)gridDim.x, p)) gather_row(u + (int)gridDim.x);
         bool stop = false;
-        if (bulk && r == 0 && u + (int)gridDim.x < units) {
+        if (bulk && r == 0 && unit_exists(u + (int)gridDim.x, p)) {
             if (wait_bar(bar(kBarStageRead), uc & 1u, abort_flag, p, 13)) {
                 issue_stage(u + (int)gridDim.x);
                 ++staged_issued;
@@ -763,7 +780,7 @@ __device__ __noinline__ void converter_warps(const HeadParams& p, uint32_t base,
     auto expand_tile = [&](uint32_t cc) -> bool { return expand_int8_tile(p, base, gbase, cc, warp & 3, lane); };
     if (!p.expand) {
         uint32_t uc = 0;
-        for (int u = blockIdx.x; u < units; u += gridDim.x, ++uc)
+        for (int u = blockIdx.x; unit_exists(u, p); u += gridDim.x, ++uc)
             if (!convert_unit(u, uc)) break;
     } else {
         // One ordered sequence of tile expansions with each unit's A conversion inserted
@@ -775,10 +792,10 @@ __device__ __noinline__ void converter_warps(const HeadParams& p, uint32_t base,
         uint32_t auc = 0, a_first = 0;  // its number within this CTA, its first tile number
         uint32_t cc = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        for (int u = blockIdx.x; ok && unit_exists(u, p); u += gridDim.x) {
             const Unit U = unit_of(u, p);
             for (int c = U.c0; ok && c < U.c1; ++c, ++cc) {
-                if (au < units && cc == a_first + (uint32_t)kStages8 - 1u) {
+                if (unit_exists(au, p) && cc == a_first + (uint32_t)kStages8 - 1u) {
                     const Unit A = unit_of(au, p);
                     ok = convert_unit(au, auc);
                     a_first += (uint32_t)(A.c1 - A.c0);
@@ -788,7 +805,7 @@ __device__ __noinline__ void converter_warps(const HeadParams& p, uint32_t base,
                 ok = ok && expand_tile(cc);
             }
         }
-        for (; ok && au < units; au += gridDim.x, ++auc) ok = convert_unit(au, auc);
+        for (; ok && unit_exists(au, p); au += gridDim.x, ++auc) ok = convert_unit(au, auc);
     }
     // a staged copy still in flight must land before the CTA exits
     if (bulk && r == 0 && staged_issued > staged_used) drain_bar(bar(kBarStageFull), (staged_issued - 1) & 1u, p);
@@ -803,7 +820,6 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
     uint32_t* qflag_s = reinterpret_cast<uint32_t*>(gbase + kOffQFlag);
     float4* merge_s = reinterpret_cast<float4*>(gbase + kOffMerge);
     auto bar = [&](int i) -> uint32_t { return base + kOffBars + 8u * (uint32_t)i; };
-    const int units = p.n_mblocks * p.n_splits;
     // ------------------------------------------------------------- epilogue
     // A group takes a 64-column half of a tile: two 32-column TMEM loads, each followed by
     // its math from registers; the accumulator goes back to the MMA issuer once both halves'
@@ -817,7 +833,7 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint32_t cc0 = 0, uc = 0;  // tiles before this unit, units so far
     bool ok = true;
-    for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
+    for (int u = blockIdx.x; ok && unit_exists(u, p); u += gridDim.x, ++uc) {
         const Unit U = unit_of(u, p);
         const uint32_t ntile = (uint32_t)(U.c1 - U.c0);
         const uint32_t slot = uc & 3u;
@@ -933,11 +949,12 @@ __device__ __noinline__ void epilogue_warps(const HeadParams& p, uint32_t base, 
                 }
                 if (I == 0x7fffffff) I = 0;  // no class at all (cannot happen for a real unit)
                 if (row < p.m) {
-                    if (p.n_splits == 1) {
+                    if (U.mb < p.whole_units || p.n_splits == 1) {
                         p.idx[row] = I;
                         p.prob[row] = 1.0f / S;
-                    } else {
-                        p.partial[(size_t)U.sp * (size_t)p.m + (size_t)row] =
+                    } else {  // rows of the split row blocks, from row 128 whole_units on
+                        const long long row0 = (long long)p.whole_units * kBlockM;
+                        p.partial[(size_t)U.sp * (size_t)(p.m - row0) + (size_t)(row - row0)] =
                             make_float4(M, S, __int_as_float(I), 0.0f);
                     }
                 }
@@ -968,7 +985,6 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int units = p.n_mblocks * p.n_splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kMaxStages; ++s) {
@@ -1027,7 +1043,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         const int bar_empty = p.expand ? kBarI8Empty : kBarBEmpty;
         uint32_t cc = 0, issued = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        for (int u = blockIdx.x; ok && unit_exists(u, p); u += gridDim.x) {
             const Unit U = unit_of(u, p);
             for (int c = U.c0; c < U.c1; ++c, ++cc) {
                 const int s = (int)(cc % ring);
@@ -1075,7 +1091,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         const uint32_t a_tmem = tmem + kTmemA;
         uint32_t s = 0, sph = 0, buf = 0, aph = 0, uc = 0;
         bool ok = true;
-        for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++uc) {
+        for (int u = blockIdx.x; ok && unit_exists(u, p); u += gridDim.x, ++uc) {
             const Unit U = unit_of(u, p);
             ok = __all_sync(0xffffffffu, wait_bar(bar(kBarAFull), uc & 1u, abort_flag, p, 2));
             if (!ok) break;
@@ -1149,7 +1165,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) head_kernel(const __grid_cons
         if (!EMIT_LOGITS) {
             uint32_t cc = 0, pending = 0;  // pending: 1 + slot of a copy not yet seen landing
             bool ok = true;
-            for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+            for (int u = blockIdx.x; ok && unit_exists(u, p); u += gridDim.x) {
                 const Unit U = unit_of(u, p);
                 for (int c = U.c0; c < U.c1; ++c, ++cc) {
                     const uint32_t slot = cc % kCtabSlots;

@@ -162,6 +162,7 @@ UNIT_SHAPES = {
     "ragged": [2, 3, 1, 5, 8, 2, 1, 1, 13],
     "tiny head (K=80, N=6906)": [55] * 9,
     "split plans": [9] * 17 + [3],
+    "cfg2 plan (six whole row blocks, then a split one)": [147] * 6 + [74],
 }
 
 

@@ -65,18 +65,15 @@ def test_no_alloc_entry_point_matches_allocating_entry_point_twice():
     with rh.Context(devices=[0]) as ctx:
         qw = rh.QuantizedWeight.from_f32_transposed(w_t, ctx=ctx, bias=bias)
         stream = torch.cuda.current_stream().cuda_stream
-        # 1000 rows: 8 row blocks, the class range split ~18 ways; 122,880 rows (cfg2): 2 ways.
-        # Both plans write their partials to the static array; the second one fills most of it.
-        # 100,000 rows: the planner's 3 ways would need 300,000 entries, so the call coarsens
-        # to 2 longer class ranges; 140,000 rows: 2 ways would need 280,000, so it runs the
-        # whole class range per row block and launches no merge; 262,144 rows: the limit.
+        # 1000 rows: 8 row blocks, each split into 17 class ranges. From one wave of row blocks
+        # on, full waves of whole row blocks, then the rest split: 122,880 rows (cfg2) 72
+        # blocks in 2 ranges, 100,000 rows 42 blocks in 7, 140,000 rows 58 blocks in 5, and
+        # 262,144 rows (the limit) 124 blocks in 7, whose partials (111,104 entries) fill most
+        # of the static array. Every one writes partials and launches the head and a merge.
         for rows in (1000, 122880, 100000, 140000, NOALLOC_MAX_ROWS):
             x = torch.from_numpy(rng.standard_normal((rows, workloads.K), dtype=np.float32)).cuda()
             launches = _compare_twice(rh, lib, ctx, qw, x, rows, stream, "int8")
-            if rows == 140000:
-                assert launches == 1, "the coarsened call still launched a merge"
-            elif rows == 100000:
-                assert launches == 2
+            assert launches == 2, f"rows={rows}: {launches} launches per call (head and merge expected)"
         # beyond the static limit: a clear error and nothing launched
         before = ctx.launch_count(0)
         x = torch.zeros((8, workloads.K), dtype=torch.float32, device="cuda")
