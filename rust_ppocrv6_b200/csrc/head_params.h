@@ -120,9 +120,9 @@ struct RecParams {
     long long n_lines;
     int out_h;           // rows per line (target height, at least 1)
     int wmax;            // columns per line in the output (the largest resized width)
-    int span_cap;        // staged columns (shared memory: span_cap float4)
+    int span_cap;        // staged columns (shared memory: three f32 planes of span_cap)
     int meta_cap;        // column windows staged per block (0: none; lines with kx > 0, one chunk and
-                         // out_w <= meta_cap stage theirs: int + float4 each)
+                         // out_w <= meta_cap stage theirs: float4 + f32 each)
     int2* coords;        // tap windows, trimmed to their non-zero weights
     float* wts;          // normalised tap weights
     float* out;          // [n_lines][3][out_h][wmax]

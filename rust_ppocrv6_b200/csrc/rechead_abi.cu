@@ -699,7 +699,7 @@ void rec_describe(const int64_t* offs, const uint32_t* widths, const uint32_t* h
         n_wts += (long long)L.out_w * L.stride_x + (long long)b.out_h * L.stride_y;
     }
     // the staged windows share the block's shared memory with the span stage (227 KB per block)
-    if ((long long)span_cap * 16 + (long long)meta_cap * 20 > 200 * 1024) meta_cap = 0;
+    if ((3LL * span_cap + 3) / 4 * 16 + (long long)meta_cap * 20 > 200 * 1024) meta_cap = 0;
 }
 
 // Byte range [lo, hi) of the non-empty crops among lines [l0, l1) (lo == hi when none).

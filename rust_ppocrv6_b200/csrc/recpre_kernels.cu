@@ -25,15 +25,15 @@
 //   rec_resize_kernel   one block per (line, 8 output rows). The white padding first; then per
 //                       row and chunk of output columns (the whole line unless its input span is
 //                       very wide): the vertical pass of the chunk's input columns into shared
-//                       memory (one float4 per column, taps unrolled for the row's tap count,
-//                       weights in registers), then the horizontal pass (unrolled to the line's
-//                       bound kx, float4 weights), writing the three normalised planes
-//                       (coalesced). A one-chunk line with kx > 0 stages its column windows in
-//                       shared memory once for all 8 rows (they do not depend on the row). Each
-//                       crop byte is read from DRAM about once (rows shared with neighbouring
-//                       blocks come from L2) and each output float is written once; the kernel is
-//                       bound by instruction issue, not by HBM (measured: ~64% issue-active,
-//                       ~25% of HBM bandwidth).
+//                       memory (three f32 planes, taps unrolled for the row's tap count, weights
+//                       in registers), then the horizontal pass (unrolled to the line's bound kx),
+//                       writing the three normalised planes (coalesced). A one-chunk line with
+//                       kx > 0 stages its column windows in shared memory once for all 8 rows
+//                       (they do not depend on the row): one 16-byte record per column. Each crop
+//                       byte is read from DRAM about once (rows shared with neighbouring blocks
+//                       come from L2) and each output float is written once; the kernel is bound
+//                       by the L1 / shared-memory data pipe (the byte loads, the stage and its
+//                       reads), not by HBM.
 #include <cstdint>
 
 #include "head_params.h"
@@ -109,23 +109,50 @@ __device__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, floa
 }
 
 // Clamp to 255 (the sum is never negative), round half away from zero (the u8 of the resized
-// image), normalise.
+// image), normalise. The rounding is one fused multiply-add rounding toward -inf:
+// 24929 * 336.5 = 2^23 + 1/2 exactly, so for 0 <= t <= 255 the exact value 2^23 + 1/2 + t lies
+// in [2^23, 2^24), where the floats are the integers, and rounding it down gives
+// 2^23 + floor(t + 1/2) = 2^23 + round(t) (a tie goes up, i.e. away from zero, for t >= 0).
+// Removing 2^23 is exact.
 __device__ __forceinline__ float to_unit(float t, float inv) {
     t = fminf(t, 255.0f);
-    return __fsub_rn(__fmul_rn(roundf(t), inv), 1.0f);
+    const float n = __fadd_rn(__fmaf_rd(24929.0f, 336.5f, t), -8388608.0f);
+    return __fsub_rn(__fmul_rn(n, inv), 1.0f);
 }
 
-// p * w added to a float4 channel accumulator (the first tap sets it).
-__device__ __forceinline__ void tap(float4& a, float4 p, float w, bool first) {
+// The vertical-pass stage in shared memory: one f32 plane per channel, span_cap columns each
+// (three 4-byte reads per tap: a warp's taps spread over about 32 s consecutive columns, so
+// each read costs at most ceil(s) bank passes, and no lane of padding is moved).
+struct Stage {
+    float* r;
+    float* g;
+    float* b;
+};
+
+// (pr, pg, pb) * w added to a channel accumulator (the first tap sets it).
+__device__ __forceinline__ void tap(float4& a, float pr, float pg, float pb, float w, bool first) {
     if (first) {
-        a.x = __fmul_rn(p.x, w);
-        a.y = __fmul_rn(p.y, w);
-        a.z = __fmul_rn(p.z, w);
+        a.x = __fmul_rn(pr, w);
+        a.y = __fmul_rn(pg, w);
+        a.z = __fmul_rn(pb, w);
     } else {
-        a.x = __fadd_rn(a.x, __fmul_rn(p.x, w));
-        a.y = __fadd_rn(a.y, __fmul_rn(p.y, w));
-        a.z = __fadd_rn(a.z, __fmul_rn(p.z, w));
+        a.x = __fadd_rn(a.x, __fmul_rn(pr, w));
+        a.y = __fadd_rn(a.y, __fmul_rn(pg, w));
+        a.z = __fadd_rn(a.z, __fmul_rn(pb, w));
     }
+}
+
+__device__ __forceinline__ void tap(float4& a, float4 p, float w, bool first) { tap(a, p.x, p.y, p.z, w, first); }
+
+// Staged column c as a tap.
+__device__ __forceinline__ void tap(float4& a, const Stage& st, int c, float w, bool first) {
+    tap(a, st.r[c], st.g[c], st.b[c], w, first);
+}
+
+__device__ __forceinline__ void put(const Stage& st, int c, const float4& a) {
+    st.r[c] = a.x;
+    st.g[c] = a.y;
+    st.b[c] = a.z;
 }
 
 __device__ __forceinline__ float4 px3(const uint8_t* __restrict__ p) {
@@ -136,14 +163,14 @@ __device__ __forceinline__ float4 px3(const uint8_t* __restrict__ p) {
 // `top` (NY == 0: any count, loop). Each thread takes U columns per step, loading all their
 // bytes before the arithmetic so that the loads overlap.
 template <int NY, int U>
-__device__ __forceinline__ void vpass(float4* __restrict__ vs, const uint8_t* __restrict__ top, size_t pitch,
-                                      int left0, int span, const float* __restrict__ wy, int ny) {
+__device__ __forceinline__ void vpass(const Stage st, const uint8_t* __restrict__ top, size_t pitch, int left0,
+                                      int span, const float* __restrict__ wy, int ny) {
     if constexpr (NY == 0) {
         for (int c = threadIdx.x; c < span; c += kRecThreads) {
             const uint8_t* __restrict__ q = top + (size_t)(left0 + c) * 3;
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int j = 0; j < ny; ++j) tap(a, px3(q + j * pitch), __ldg(wy + j), j == 0);
-            vs[c] = a;
+            put(st, c, a);
         }
     } else {
         float w[NY];
@@ -163,7 +190,7 @@ __device__ __forceinline__ void vpass(float4* __restrict__ vs, const uint8_t* __
                 float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                 for (int j = 0; j < NY; ++j) tap(a, v[u][j], w[j], j == 0);
-                if (c0 + u * kRecThreads < span) vs[c0 + u * kRecThreads] = a;
+                if (c0 + u * kRecThreads < span) put(st, c0 + u * kRecThreads, a);
             }
         }
     }
@@ -172,8 +199,8 @@ __device__ __forceinline__ void vpass(float4* __restrict__ vs, const uint8_t* __
 // Horizontal pass of output columns [x0, x1): at most KX taps per column (KX == 0: any
 // count). Each thread takes U columns per step, loading their windows first.
 template <int KX, int U>
-__device__ __forceinline__ void hpass(const RecParams& p, const RecLine& L, const float4* __restrict__ vs, int left0,
-                                      int span, int x0, int x1, float* r0, float* r1, float* r2) {
+__device__ __forceinline__ void hpass(const RecParams& p, const RecLine& L, const Stage st, int left0, int span,
+                                      int x0, int x1, float* r0, float* r1, float* r2) {
     const int last = span - 1;
     for (int xb = x0 + (int)threadIdx.x; xb < x1; xb += U * kRecThreads) {
         int2 cx[U];
@@ -197,10 +224,10 @@ __device__ __forceinline__ void hpass(const RecParams& p, const RecLine& L, cons
             if (KX > 0 && cx[u].y <= KX) {
                 const float wv[4] = {w4[u].x, w4[u].y, w4[u].z, w4[u].w};
 #pragma unroll
-                for (int j = 0; j < (KX > 0 ? KX : 1); ++j) tap(a, vs[min(base + j, last)], wv[j], j == 0);
+                for (int j = 0; j < (KX > 0 ? KX : 1); ++j) tap(a, st, min(base + j, last), wv[j], j == 0);
             } else {
                 const float* __restrict__ wx = p.wts + L.wts + (long long)x * L.stride_x;
-                for (int j = 0; j < cx[u].y; ++j) tap(a, vs[base + j], __ldg(wx + j), j == 0);
+                for (int j = 0; j < cx[u].y; ++j) tap(a, st, base + j, __ldg(wx + j), j == 0);
             }
             r0[x] = to_unit(a.x, p.inv);
             r1[x] = to_unit(a.y, p.inv);
@@ -210,25 +237,26 @@ __device__ __forceinline__ void hpass(const RecParams& p, const RecLine& L, cons
 }
 
 // Horizontal pass of a whole line (one chunk) whose column windows were staged once per block:
-// mb[x] = first tap relative to the staged span, mw[x] = its weights, zero-padded to 4 (a window
-// that failed its check has weight 0 and raised the status flag). The stage holds 4 zero columns
-// past the span, so a padded tap reads a finite value and adds exactly 0. Branch-free: the last
-// step's spare lanes recompute column out_w - 1 and do not store.
+// mrec[x] = (first tap relative to the staged span, as int bits; weights 0..2), mw3[x] = weight 3,
+// zero-padded (a window that failed its check has weight 0 and raised the status flag): one
+// 16-byte read per column for KX <= 3. The stage holds 4 zero columns past the span, so a padded
+// tap reads a finite value and adds exactly 0. Branch-free: the last step's spare lanes
+// recompute column out_w - 1 and do not store.
 template <int KX, int U>
-__device__ __forceinline__ void hpass_staged(const float4* __restrict__ vs, const int* __restrict__ mb,
-                                             const float4* __restrict__ mw, int out_w, float inv, float* r0,
+__device__ __forceinline__ void hpass_staged(const Stage st, const float4* __restrict__ mrec,
+                                             const float* __restrict__ mw3, int out_w, float inv, float* r0,
                                              float* r1, float* r2) {
     for (int xb = (int)threadIdx.x; xb < out_w; xb += U * kRecThreads) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int x = xb + u * kRecThreads;
             const int xc = min(x, out_w - 1);
-            const int base = mb[xc];
-            const float4 w4 = mw[xc];
-            const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+            const float4 m = mrec[xc];
+            const int base = __float_as_int(m.x);
+            const float wv[4] = {m.y, m.z, m.w, KX > 3 ? mw3[xc] : 0.0f};
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int j = 0; j < KX; ++j) tap(a, vs[base + j], wv[j], j == 0);
+            for (int j = 0; j < KX; ++j) tap(a, st, base + j, wv[j], j == 0);
             if (x < out_w) {
                 r0[x] = to_unit(a.x, inv);
                 r1[x] = to_unit(a.y, inv);
@@ -256,9 +284,12 @@ __global__ void __launch_bounds__(kRecThreads) rec_weights_kernel(const RecParam
 }
 
 __global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecParams p, long long line0) {
-    // [span_cap] vertical-pass values (r, g, b, -) of the chunk's columns; then, for the staged
-    // column windows, float4 [meta_cap] weights and int [meta_cap] first taps
-    extern __shared__ float4 vs[];
+    // three f32 planes [span_cap]: the vertical-pass values (r, g, b) of the chunk's columns; then,
+    // 16-byte aligned, for the staged column windows float4 [meta_cap] records and f32 [meta_cap]
+    // fourth weights
+    extern __shared__ float4 smem[];
+    float* const planes = reinterpret_cast<float*>(smem);
+    const Stage st{planes, planes + p.span_cap, planes + 2 * p.span_cap};
     const int groups = (p.out_h + kRecRows - 1) / kRecRows;
     const long long li = line0 + blockIdx.x / groups;
     const int y0 = (int)(blockIdx.x % groups) * kRecRows, y1 = min(y0 + kRecRows, p.out_h);
@@ -280,8 +311,8 @@ __global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecPar
     if (L.kx > 0 && L.chunk == L.out_w && L.out_w <= p.meta_cap) {
         // One chunk per row and at most kx taps per column: the column windows do not depend on
         // the row, so they are staged once for the block's rows.
-        float4* mw = vs + p.span_cap;  // float4 first: keeps 16-byte alignment for any meta_cap
-        int* mb = reinterpret_cast<int*>(mw + p.meta_cap);
+        float4* mrec = smem + (3 * p.span_cap + 3) / 4;
+        float* mw3 = reinterpret_cast<float*>(mrec + p.meta_cap);
         const int2 a = p.coords[L.coord], b = p.coords[L.coord + L.out_w - 1];
         const int left0 = a.x, span = b.x + b.y - a.x;
         if (span <= 0 || span + 4 > p.span_cap) {  // same values in every thread: the whole block leaves
@@ -293,11 +324,12 @@ __global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecPar
             const int base = cx.x - left0;
             const bool ok = base >= 0 && base + cx.y <= span && cx.y <= L.kx;
             if (!ok) flag(p.status);
-            mb[x] = ok ? base : 0;
-            mw[x] = ok ? __ldg(reinterpret_cast<const float4*>(p.wts + L.wts + (long long)x * L.stride_x))
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 w = ok ? __ldg(reinterpret_cast<const float4*>(p.wts + L.wts + (long long)x * L.stride_x))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            mrec[x] = make_float4(__int_as_float(ok ? base : 0), w.x, w.y, w.z);
+            mw3[x] = w.w;
         }
-        if (threadIdx.x < 4) vs[span + threadIdx.x] = make_float4(0.f, 0.f, 0.f, 0.f);  // tap padding
+        if (threadIdx.x < 4) put(st, span + threadIdx.x, make_float4(0.f, 0.f, 0.f, 0.f));  // tap padding
         for (int y = y0; y < y1; ++y) {
             const int2 cy = p.coords[L.coord + L.out_w + y];
             const float* __restrict__ wy = p.wts + L.wts + (long long)L.out_w * L.stride_x + (long long)y * L.stride_y;
@@ -305,17 +337,17 @@ __global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecPar
             float* r0 = line_out + (size_t)y * (size_t)p.wmax;
             if (y > y0) __syncthreads();  // the previous horizontal pass is done with the stage
             switch (cy.y) {
-                case 1: vpass<1, 2>(vs, top, pitch, left0, span, wy, 1); break;
-                case 2: vpass<2, 2>(vs, top, pitch, left0, span, wy, 2); break;
-                case 3: vpass<3, 2>(vs, top, pitch, left0, span, wy, 3); break;
-                case 4: vpass<4, 1>(vs, top, pitch, left0, span, wy, 4); break;
-                default: vpass<0, 1>(vs, top, pitch, left0, span, wy, cy.y); break;
+                case 1: vpass<1, 4>(st, top, pitch, left0, span, wy, 1); break;
+                case 2: vpass<2, 4>(st, top, pitch, left0, span, wy, 2); break;
+                case 3: vpass<3, 2>(st, top, pitch, left0, span, wy, 3); break;
+                case 4: vpass<4, 1>(st, top, pitch, left0, span, wy, 4); break;
+                default: vpass<0, 1>(st, top, pitch, left0, span, wy, cy.y); break;
             }
-            __syncthreads();  // also publishes mb / mw before the first row's horizontal pass
+            __syncthreads();  // also publishes mrec / mw3 before the first row's horizontal pass
             switch (L.kx) {
-                case 2: hpass_staged<2, 2>(vs, mb, mw, L.out_w, p.inv, r0, r0 + plane, r0 + 2 * plane); break;
-                case 3: hpass_staged<3, 2>(vs, mb, mw, L.out_w, p.inv, r0, r0 + plane, r0 + 2 * plane); break;
-                default: hpass_staged<4, 2>(vs, mb, mw, L.out_w, p.inv, r0, r0 + plane, r0 + 2 * plane); break;
+                case 2: hpass_staged<2, 1>(st, mrec, mw3, L.out_w, p.inv, r0, r0 + plane, r0 + 2 * plane); break;
+                case 3: hpass_staged<3, 1>(st, mrec, mw3, L.out_w, p.inv, r0, r0 + plane, r0 + 2 * plane); break;
+                default: hpass_staged<4, 1>(st, mrec, mw3, L.out_w, p.inv, r0, r0 + plane, r0 + 2 * plane); break;
             }
         }
         return;
@@ -337,18 +369,18 @@ __global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecPar
             }
             if (y > y0 || x0 > 0) __syncthreads();  // the previous horizontal pass is done with the stage
             switch (cy.y) {
-                case 1: vpass<1, 2>(vs, top, pitch, left0, span, wy, 1); break;
-                case 2: vpass<2, 2>(vs, top, pitch, left0, span, wy, 2); break;
-                case 3: vpass<3, 2>(vs, top, pitch, left0, span, wy, 3); break;
-                case 4: vpass<4, 1>(vs, top, pitch, left0, span, wy, 4); break;
-                default: vpass<0, 1>(vs, top, pitch, left0, span, wy, cy.y); break;
+                case 1: vpass<1, 4>(st, top, pitch, left0, span, wy, 1); break;
+                case 2: vpass<2, 4>(st, top, pitch, left0, span, wy, 2); break;
+                case 3: vpass<3, 2>(st, top, pitch, left0, span, wy, 3); break;
+                case 4: vpass<4, 1>(st, top, pitch, left0, span, wy, 4); break;
+                default: vpass<0, 1>(st, top, pitch, left0, span, wy, cy.y); break;
             }
             __syncthreads();
             switch (L.kx) {
-                case 2: hpass<2, 2>(p, L, vs, left0, span, x0, x1, r0, r1, r2); break;
-                case 3: hpass<3, 2>(p, L, vs, left0, span, x0, x1, r0, r1, r2); break;
-                case 4: hpass<4, 2>(p, L, vs, left0, span, x0, x1, r0, r1, r2); break;
-                default: hpass<0, 1>(p, L, vs, left0, span, x0, x1, r0, r1, r2); break;
+                case 2: hpass<2, 2>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
+                case 3: hpass<3, 2>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
+                case 4: hpass<4, 2>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
+                default: hpass<0, 1>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
             }
         }
     }
@@ -363,7 +395,8 @@ cudaError_t launch_rec_weights(const RecParams& p, cudaStream_t stream) {
 
 cudaError_t launch_rec_resize(const RecParams& p, long long line0, long long n, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
-    const size_t smem = (size_t)p.span_cap * sizeof(float4) + (size_t)p.meta_cap * (sizeof(int) + sizeof(float4));
+    const size_t smem = (size_t)((3 * p.span_cap + 3) / 4) * sizeof(float4) +
+                        (size_t)p.meta_cap * (sizeof(float4) + sizeof(float));
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(rec_resize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;

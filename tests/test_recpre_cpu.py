@@ -176,3 +176,57 @@ def test_batch_shape_rejects_unsupported_sizes(rh):
     with pytest.raises(rh.RecHeadError) as e:
         rh.batch_shape([600_000], [900_000])
     assert e.value.code == rh.RH_ERR_UNSUPPORTED
+
+
+# --------------------------------------------- the kernel's rounding step, checked exhaustively
+
+_ROUNDING_C = r"""
+#include <fenv.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#pragma STDC FENV_ACCESS ON
+/* For every float t in [+0, 255]: fma(24929, 336.5, t) rounded toward -inf, minus 2^23,
+   against roundf(t) (half away from zero). argv[1] = "down" or "nearest"; argv[2], argv[3] =
+   the bit patterns of the first and the last t. */
+int main(int argc, char** argv) {
+    volatile float a = 24929.0f, b = 336.5f, bias = 8388608.0f;
+    unsigned long long n = 0, bad = 0;
+    if (fesetround(strcmp(argv[1], "down") == 0 ? FE_DOWNWARD : FE_TONEAREST) != 0) return 2;
+    const uint32_t first = (uint32_t)strtoul(argv[2], NULL, 16), last = (uint32_t)strtoul(argv[3], NULL, 16);
+    for (uint32_t u = first; u <= last; ++u) {
+        float t;
+        memcpy(&t, &u, 4);
+        if (fmaf(a, b, t) - bias != roundf(t)) ++bad;
+        ++n;
+    }
+    printf("%llu %llu\n", n, bad);
+    return 0;
+}
+"""
+
+
+def test_kernel_rounding_step_is_round_half_away_for_every_float(tmp_path):
+    """The resize kernel rounds the clamped horizontal sum t (0 <= t <= 255) as
+    fma(24929, 336.5, t) with rounding toward -inf, minus 2^23: 24929 * 336.5 = 2^23 + 1/2, the
+    exact value lands among the integers of [2^23, 2^24), and rounding it down is
+    floor(t + 1/2). This checks the identity against roundf for all 1,132,396,545 floats of
+    [+0, 255], with the C library's correctly rounded fmaf standing for the GPU's fma.rm; in
+    round-to-nearest the same formula is wrong (t = 0.25 gives 1), which shows the check can fail."""
+    import shutil
+    import subprocess
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not found")
+    src, exe = tmp_path / "rounding.c", tmp_path / "rounding"
+    src.write_text(_ROUNDING_C)
+    subprocess.run([gcc, "-O2", "-frounding-math", "-o", str(exe), str(src), "-lm"], check=True)
+    n, bad = map(int, subprocess.run([str(exe), "down", "0", "437F0000"], check=True, capture_output=True,
+                                     text=True).stdout.split())
+    assert (n, bad) == (0x437F0000 + 1, 0)
+    n, bad = map(int, subprocess.run([str(exe), "nearest", "3E800000", "3E8000FF"], check=True,
+                                     capture_output=True, text=True).stdout.split())  # 256 floats from 0.25
+    assert n == 256 and bad > 0
