@@ -17,7 +17,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "librechead.so")
 SOURCES = ["rechead_kernels.cu", "ctc_kernels.cu", "recpre_kernels.cu", "rechead_abi.cu"]
-HEADERS = ["head_params.h", "sm100_ptx.cuh"]
+HEADERS = ["head_params.h", "recpre_params.h", "sm100_ptx.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include "head_params.h"
+#include "recpre_params.h"
 #include "rechead.h"
 
 namespace {
@@ -582,10 +583,10 @@ int kt_ctc_on_slot(rh_ctx* ctx, const rh_weight* w, int slot, const float* x, in
 }
 
 // ------------------------------------------------------ recognition preprocessing
-// Target staged span when choosing a line's chunk (32 KB of shared memory per block); lines
+// Target staged span when choosing a line's chunk (24 KB of shared memory per block); lines
 // that downscale so much that even one output column needs more than rh::kRecSpanMax input
 // columns are rejected as unsupported.
-constexpr double kRecSpanTarget = 2048.0;  // 32 KB of float4
+constexpr double kRecSpanTarget = 2048.0;  // three f32 planes: 24 KB
 constexpr uint32_t kRecMaxDim = 1u << 30;   // crop sides above this are rejected
 constexpr uint32_t kRecMaxHeight = 1u << 20;  // target heights above this are rejected
 
@@ -676,8 +677,8 @@ void rec_describe(const int64_t* offs, const uint32_t* widths, const uint32_t* h
         L.src = offs[l] - base;
         const double rx = (double)L.w / L.out_w, sx = std::max(rx, 1.0);
         const double ry = (double)L.h / b.out_h, sy = std::max(ry, 1.0);
-        // columns of a line that shrinks by at most 2x have at most ceil(2 s) <= 4 non-zero taps
-        // (and at most 2 s + 2 <= 6 before trimming): a padded, 16-byte aligned slot of 8
+        // columns of a line that shrinks by at most 2x have at most ceil(2 s) <= 4 non-zero taps:
+        // a zero-padded, 16-byte aligned slot of 4 (the window is trimmed in registers first)
         L.kx = sx <= 2.0 ? (int)std::ceil(2.0 * sx) : 0;
         L.stride_x = L.kx > 0 ? rh::kRecFastSlots : (int)std::ceil(2.0 * sx) + 3;
         L.stride_y = (int)std::ceil(2.0 * sy) + 3;

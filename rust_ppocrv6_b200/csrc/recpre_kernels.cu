@@ -37,6 +37,7 @@
 #include <cstdint>
 
 #include "head_params.h"
+#include "recpre_params.h"
 
 namespace rh {
 
@@ -49,8 +50,11 @@ __device__ __forceinline__ void flag(int* status) { atomicOr(status, kDevRecPlan
 // Tap window of output coordinate o, trimmed to its non-zero weights: returns (first tap,
 // count) and leaves the normalised weights in w[0..count), zeros in w[count..pad).
 // Windows of up to 8 taps (every axis that shrinks by at most 3x) are computed in registers
-// and written once; wider ones go through w itself.
-__device__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, float* __restrict__ w, int* status) {
+// and written once; wider ones go through w itself. The slots hold at least the trimmed window
+// (stride >= count); the loop for wider windows needs the untrimmed one (stride >= hi - lo).
+// A slot of exactly 4 (pad == stride == 4) is written whole by one 16-byte store, so the L2
+// never has to merge a partly written sector with DRAM.
+__device__ __forceinline__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, float* __restrict__ w, int* status) {
     const float ratio = __fdiv_rn((float)n_in, (float)n_out);
     const float s = ratio < 1.0f ? 1.0f : ratio;
     const float centre = __fmul_rn(__fadd_rn((float)o, 0.5f), ratio);
@@ -60,7 +64,7 @@ __device__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, floa
     hi = hi < lo + 1 ? lo + 1 : hi;
     hi = hi > n_in ? n_in : hi;
     int cnt = (int)(hi - lo);
-    if (cnt > stride) {  // the host sized the slots from 2s + 3; never expected
+    if (cnt > 8 && cnt > stride) {  // the host sized the slots from 2s + 3; never expected
         flag(status);
         cnt = stride;
     }
@@ -80,14 +84,32 @@ __device__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, floa
 #pragma unroll
         for (int j = 0; j < 8; ++j) j1 = r[j] != 0.0f ? j : j1;
         if (j1 < j0) j0 = j1 = 0;  // no non-zero tap (a zero sum; never expected): keep one
-        const int n = j1 - j0 + 1;
+        int n = j1 - j0 + 1;
+        if (n > stride) {  // a kx > 0 slot holds ceil(2 s) >= n taps; never expected
+            flag(status);
+            n = stride;
+        }
         const int m = max(n, min(pad, stride));  // slots to write
+        // q = r shifted down by j0, in three conditional steps of 1, 2 and 4 (every index is a
+        // constant, so r and q stay in registers)
+        float q[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            float v = 0.0f;
+        for (int k = 0; k < 8; ++k) q[k] = r[k];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v = (j == k + j0) ? r[j] : v;
-            if (k < m) w[k] = k < n ? __fdiv_rn(v, sum) : 0.0f;
+        for (int st = 1; st < 8; st <<= 1) {
+            if (j0 & st) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) q[k] = k + st < 8 ? q[k + st] : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) q[k] = k < n ? __fdiv_rn(q[k], sum) : 0.0f;
+        if (pad == 4 && stride == 4) {
+            *reinterpret_cast<float4*>(w) = make_float4(q[0], q[1], q[2], q[3]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (k < m) w[k] = q[k];
         }
         return make_int2((int)lo + j0, n);
     }
@@ -283,7 +305,7 @@ __global__ void __launch_bounds__(kRecThreads) rec_weights_kernel(const RecParam
     }
 }
 
-__global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecParams p, long long line0) {
+__global__ void __launch_bounds__(kRecThreads, 6) rec_resize_kernel(const RecParams p, long long line0) {
     // three f32 planes [span_cap]: the vertical-pass values (r, g, b) of the chunk's columns; then,
     // 16-byte aligned, for the staged column windows float4 [meta_cap] records and f32 [meta_cap]
     // fourth weights
@@ -337,8 +359,8 @@ __global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecPar
             float* r0 = line_out + (size_t)y * (size_t)p.wmax;
             if (y > y0) __syncthreads();  // the previous horizontal pass is done with the stage
             switch (cy.y) {
-                case 1: vpass<1, 4>(st, top, pitch, left0, span, wy, 1); break;
-                case 2: vpass<2, 4>(st, top, pitch, left0, span, wy, 2); break;
+                case 1: vpass<1, 2>(st, top, pitch, left0, span, wy, 1); break;
+                case 2: vpass<2, 2>(st, top, pitch, left0, span, wy, 2); break;
                 case 3: vpass<3, 2>(st, top, pitch, left0, span, wy, 3); break;
                 case 4: vpass<4, 1>(st, top, pitch, left0, span, wy, 4); break;
                 default: vpass<0, 1>(st, top, pitch, left0, span, wy, cy.y); break;
@@ -369,17 +391,17 @@ __global__ void __launch_bounds__(kRecThreads, 5) rec_resize_kernel(const RecPar
             }
             if (y > y0 || x0 > 0) __syncthreads();  // the previous horizontal pass is done with the stage
             switch (cy.y) {
-                case 1: vpass<1, 4>(st, top, pitch, left0, span, wy, 1); break;
-                case 2: vpass<2, 4>(st, top, pitch, left0, span, wy, 2); break;
+                case 1: vpass<1, 2>(st, top, pitch, left0, span, wy, 1); break;
+                case 2: vpass<2, 2>(st, top, pitch, left0, span, wy, 2); break;
                 case 3: vpass<3, 2>(st, top, pitch, left0, span, wy, 3); break;
                 case 4: vpass<4, 1>(st, top, pitch, left0, span, wy, 4); break;
                 default: vpass<0, 1>(st, top, pitch, left0, span, wy, cy.y); break;
             }
             __syncthreads();
             switch (L.kx) {
-                case 2: hpass<2, 2>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
-                case 3: hpass<3, 2>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
-                case 4: hpass<4, 2>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
+                case 2: hpass<2, 1>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
+                case 3: hpass<3, 1>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
+                case 4: hpass<4, 1>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
                 default: hpass<0, 1>(p, L, st, left0, span, x0, x1, r0, r1, r2); break;
             }
         }
