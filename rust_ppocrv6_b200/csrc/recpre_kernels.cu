@@ -53,7 +53,9 @@ __device__ __forceinline__ void flag(int* status) { atomicOr(status, kDevRecPlan
 // and written once; wider ones go through w itself. The slots hold at least the trimmed window
 // (stride >= count); the loop for wider windows needs the untrimmed one (stride >= hi - lo).
 // A slot of exactly 4 (pad == stride == 4) is written whole by one 16-byte store, so the L2
-// never has to merge a partly written sector with DRAM.
+// never has to merge a partly written sector with DRAM. Divisions whose result is known
+// exactly are not carried out: those of the slots past the window, d / s when s == 1 and
+// w / sum when sum == 1.
 __device__ __forceinline__ int2 tri_window(int n_in, int n_out, int o, int stride, int pad, float* __restrict__ w, int* status) {
     const float ratio = __fdiv_rn((float)n_in, (float)n_out);
     const float s = ratio < 1.0f ? 1.0f : ratio;
@@ -74,9 +76,14 @@ __device__ __forceinline__ int2 tri_window(int n_in, int n_out, int o, int strid
         float r[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float x = fabsf(__fdiv_rn(__fsub_rn((float)(lo + j), c0), s));
-            r[j] = (j < cnt && x < 1.0f) ? __fsub_rn(1.0f, x) : 0.0f;
-            sum = __fadd_rn(sum, r[j]);  // taps past cnt add +0: the sum is unchanged
+            float rj = 0.0f;
+            if (j < cnt) {  // d / s is d exactly when s == 1 (every axis that grows)
+                const float d = __fsub_rn((float)(lo + j), c0);
+                const float x = fabsf(s == 1.0f ? d : __fdiv_rn(d, s));
+                rj = x < 1.0f ? __fsub_rn(1.0f, x) : 0.0f;
+            }
+            r[j] = rj;
+            sum = __fadd_rn(sum, rj);  // taps past cnt add +0: the sum is unchanged
         }
         int j0 = cnt, j1 = -1;  // first and last non-zero tap
 #pragma unroll
@@ -103,7 +110,10 @@ __device__ __forceinline__ int2 tri_window(int n_in, int n_out, int o, int strid
             }
         }
 #pragma unroll
-        for (int k = 0; k < 8; ++k) q[k] = k < n ? __fdiv_rn(q[k], sum) : 0.0f;
+        for (int k = 0; k < 8; ++k) {
+            if (k >= n) q[k] = 0.0f;
+            else if (sum != 1.0f) q[k] = __fdiv_rn(q[k], sum);  // v / 1 is v exactly
+        }
         if (pad == 4 && stride == 4) {
             *reinterpret_cast<float4*>(w) = make_float4(q[0], q[1], q[2], q[3]);
         } else {
