@@ -264,3 +264,20 @@ def test_randomized_batches_bit_exact(rh, ctx, oracle):
         ref, ref_w = oracle.rec_preprocess_batch(crops, th, mw, threads=8)
         assert np.array_equal(widths, ref_w), (i, dims, th, mw)
         assert_same(got, ref, f"batch {i}: {dims} H={th} max_w={mw}")
+
+
+def test_every_staged_tap_count_bit_exact(rh, ctx, oracle):
+    """One line per horizontal tap bound of the staged path: kx = ceil(2 s) is 2 (a line that
+    grows), 3 and 4 (shrinking by up to 1.5x and 2x: the fourth weight comes from its own
+    shared-memory array), and a line shrinking by more than 2x (the general path). With a
+    48-row target the horizontal ratio is about h / 48."""
+    dims = [(400, 40), (1200, 60), (1700, 85), (1900, 95), (2000, 100), (500, 30), (1300, 70)]
+    ratios = [w / min(max(int(np.ceil(48 * w / h)), 32), 2000) for w, h in dims]
+    kx = [int(np.ceil(2 * max(r, 1.0))) if max(r, 1.0) <= 2.0 else 0 for r in ratios]
+    assert {2, 3, 4, 0} <= set(kx), kx
+    for rep in range(3):
+        crops = crops_of(dims, 300 + rep)
+        got, widths = rh.RecPreprocess(48, 2000, ctx=ctx).process_batch(crops)
+        ref, ref_w = oracle.rec_preprocess_batch(crops, 48, 2000, threads=4)
+        assert np.array_equal(widths, ref_w)
+        assert_same(got, ref, f"tap bounds {kx}, seed {300 + rep}")
