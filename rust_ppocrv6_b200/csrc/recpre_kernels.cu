@@ -154,7 +154,7 @@ __device__ __forceinline__ float to_unit(float t, float inv) {
 
 // The vertical-pass stage in shared memory: one f32 plane per channel, span_cap columns each
 // (three 4-byte reads per tap: a warp's taps spread over about 32 s consecutive columns, so
-// each read costs at most ceil(s) bank passes, and no lane of padding is moved).
+// each read costs about ceil(s) bank passes, and no lane of padding is moved).
 struct Stage {
     float* r;
     float* g;
