@@ -205,18 +205,41 @@ def measured_hbm_gbs():
 KERNEL_SOURCES = ("rust_ppocrv6_b200/csrc/rechead_kernels.cu", "rust_ppocrv6_b200/csrc/sm100_ptx.cuh",
                   "rust_ppocrv6_b200/csrc/head_params.h")
 TRAFFIC_RECORD = os.path.join(ROOT, "profiles", "head_kernel_traffic.json")
+RECPRE_SOURCES = ("rust_ppocrv6_b200/csrc/recpre_kernels.cu", "rust_ppocrv6_b200/csrc/recpre_params.h")
+RECPRE_TRAFFIC_RECORD = os.path.join(ROOT, "profiles", "recpre_kernel_traffic.json")
 
 
-def kernel_source_sha16() -> str:
-    """First 16 hex digits of the SHA-256 over the head kernel's source files: a DRAM-traffic
-    figure captured by ncu applies only to the kernel built from the same sources."""
+def source_sha16(sources) -> str:
+    """First 16 hex digits of the SHA-256 over the given source files: a DRAM-traffic figure
+    captured by ncu applies only to the kernels built from the same sources."""
     import hashlib
 
     h = hashlib.sha256()
-    for rel in KERNEL_SOURCES:
+    for rel in sources:
         with open(os.path.join(ROOT, rel), "rb") as f:
             h.update(f.read())
     return h.hexdigest()[:16]
+
+
+def kernel_source_sha16() -> str:
+    """Source hash of the head kernel (rechead_kernels.cu, sm100_ptx.cuh, head_params.h)."""
+    return source_sha16(KERNEL_SOURCES)
+
+
+def recpre_traffic():
+    """(DRAM bytes read + written per preprocessing step, i.e. one tap-table and one resize
+    launch over the bench's 1,024 crops, description) from the ncu capture recorded for the
+    current preprocessing sources, or (None, reason)."""
+    try:
+        with open(RECPRE_TRAFFIC_RECORD) as f:
+            r = json.load(f)
+    except (OSError, ValueError):
+        return None, "no ncu capture recorded"
+    sha = source_sha16(RECPRE_SOURCES)
+    if r.get("source_sha16") != sha:
+        return None, f"the ncu capture is of preprocessing sources {r.get('source_sha16')}, not {sha}"
+    return int(r["dram_bytes_per_step"]), ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one rec_weights "
+                                           "and one rec_resize launch (1,024 crops)")
 
 
 def profiled_traffic(workload: str = "cfg2", weights: str = "int8"):
@@ -427,6 +450,7 @@ def run_recpre(args, world, rank, local, torch, rh, barrier, max_over_ranks):
 
     # roofline: algorithmic bytes = every crop byte read once + every output float written once
     alg_bytes = int(blob.size) + out_len * 4
+    traffic, traffic_src = recpre_traffic()
     achieved = alg_bytes / (dev_ms / args.steps / 1e3) / 1e9
     peak, peak_src = measured_hbm_gbs()
     out = {
@@ -441,7 +465,7 @@ def run_recpre(args, world, rank, local, torch, rh, barrier, max_over_ranks):
                 "d2h_bytes_per_step": int(out_len * 4), "ms_per_step": e2e_s * 1e3 / args.steps},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_src, "traffic": None,
+                     "peak_source": peak_src, "traffic": traffic, "traffic_source": traffic_src,
                      "note": "achieved = (crop bytes + output bytes) per step / device time per step (tap-table "
                              "kernel + resize kernel + descriptor copy)"},
         "clocks": clocks.summary(),

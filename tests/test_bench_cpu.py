@@ -56,6 +56,10 @@ def test_bench_helpers():
     assert (t is None and src) or t > 60_000_000
     assert len(bench.kernel_source_sha16()) == 16
     assert bench.profiled_traffic("nonexistent", "int8")[0] is None
+    # preprocessing: DRAM bytes of one step's two launches, recorded for the current sources
+    t, src = bench.recpre_traffic()
+    assert (t is None and src) or t > 600_000_000
+    assert len(bench.source_sha16(bench.RECPRE_SOURCES)) == 16
     assert np.all(np.diff(off) >= 0)
 
 
